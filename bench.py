@@ -1,0 +1,438 @@
+#!/usr/bin/env python
+"""Benchmark of the routed-expert MUL_MAT_ID hot path on B200.
+
+Workload (the config the metric is quoted on): IQ3_S
+decode of one token through 48 MoE blocks, 512 experts per block, top-10,
+hidden 2048, expert FFN 768, the whole 49.8 GB bank resident on the GPU.
+Weights are N(0, 0.02) encoded by this build's IQ3_S encoder; router logits are
+N(0,1) per layer (seed 100 + L) -> softmax -> top-10 -> renormalised; x ~ N(0,1)
+(seed 2); between blocks x <- x + y (residual). 16 routing sets (set 0 is the
+seeded one) are cycled so every step reads 973 MB of distinct expert bytes,
+more than the 126 MB L2: no L2 reuse between timed steps.
+
+A step = one token through all 48 blocks (96 kernel launches). `value` is
+device-timed (CUDA events on the launching stream, CUDA-graph replay, inputs
+resident); `e2e` goes through the public C ABI per step (sabah_moe_decode) with
+the step's inputs copied from pinned host memory and the result copied back.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (torchrun), each rank decodes its own token stream on its own bank
+replica (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+QT_IQ3_S = 21
+LAYERS, EXPERTS, D_MODEL, FF, TOP_K = 48, 512, 2048, 768, 10
+ROUTING_SETS = 16
+METRIC = "MoE MUL_MAT_ID tokens/s (IQ3_S decode, 48 x 512-expert bank resident)"
+WORKLOAD = "cfg2: IQ3_S decode, 1 token x 48 blocks, 512 experts/block, top-10, H2048 F768, 49.8 GB bank on 1 GPU"
+
+
+def iq3s_row_bytes(k: int) -> int:
+    return k // 256 * 110
+
+
+GU_ROW = iq3s_row_bytes(D_MODEL)               # 880
+D_ROW = iq3s_row_bytes(FF)                     # 330
+GU_EXPERT = FF * GU_ROW                        # 675,840
+D_EXPERT = D_MODEL * D_ROW                     # 675,840
+BYTES_PER_TOKEN = LAYERS * TOP_K * (2 * GU_EXPERT + D_EXPERT)   # 973,209,600
+
+
+def routing(n_sets: int, layers: int = LAYERS):
+    """ids/w [n_sets][layers][1][TOP_K]: softmax over N(0,1) logits, top-k, renormalised."""
+    ids = np.empty((n_sets, layers, 1, TOP_K), np.int32)
+    w = np.empty((n_sets, layers, 1, TOP_K), np.float32)
+    for s in range(n_sets):
+        for L in range(layers):
+            logits = np.random.default_rng(100 + L + 1000 * s).standard_normal(EXPERTS)
+            p = np.exp(logits - logits.max())
+            p /= p.sum()
+            top = np.argsort(-p, kind="stable")[:TOP_K]
+            ids[s, L, 0] = top
+            w[s, L, 0] = (p[top] / p[top].sum()).astype(np.float32)
+    return ids, w
+
+
+def x0():
+    return np.random.default_rng(2).standard_normal((1, D_MODEL)).astype(np.float32)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    from sabah_moe_accelerator_b200 import ops, rt
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ops.init(local_rank)
+    L = rt.lib()
+    stream = torch.cuda.Stream(device=dev)
+
+    # ---- bank: per layer [gate | up | down], each 512 experts
+    layer_bytes = EXPERTS * (2 * GU_EXPERT + D_EXPERT)
+    bank = torch.empty(LAYERS * layer_bytes, dtype=torch.uint8, device=dev)
+    gate_p, up_p, down_p = [], [], []
+    with torch.cuda.stream(stream):
+        for Lr in range(LAYERS):
+            base = Lr * layer_bytes
+            for role, off, rows, k in ((0, 0, FF, D_MODEL), (1, EXPERTS * GU_EXPERT, FF, D_MODEL),
+                                       (2, 2 * EXPERTS * GU_EXPERT, D_MODEL, FF)):
+                view = bank[base + off: base + off + EXPERTS * rows * iq3s_row_bytes(k)]
+                ops.synth_rows(EXPERTS * rows, k, QT_IQ3_S, seed=(10 + Lr) * 4 + role + 7919 * rank, sigma=0.02,
+                               out=view, stream=stream)
+                (gate_p, up_p, down_p)[role].append(view.data_ptr())
+    stream.synchronize()
+
+    ids_np, w_np = routing(ROUTING_SETS)
+    ids_d = torch.from_numpy(ids_np).to(dev)
+    w_d = torch.from_numpy(w_np).to(dev)
+    x0_d = torch.from_numpy(x0()).to(dev)
+    x_d = torch.empty_like(x0_d)
+    h_d = torch.empty((1, TOP_K, FF), dtype=torch.float32, device=dev)
+    c_arr = ctypes.c_void_p * LAYERS
+    G, U, D = c_arr(*gate_p), c_arr(*up_p), c_arr(*down_p)
+
+    def decode(s: int, st):
+        rc = L.sabah_moe_decode(LAYERS, G, U, D, GU_EXPERT, D_EXPERT, EXPERTS, ids_d[s].data_ptr(),
+                                w_d[s].data_ptr(), x_d.data_ptr(), h_d.data_ptr(), D_MODEL, FF, TOP_K, 1,
+                                QT_IQ3_S, QT_IQ3_S, QT_IQ3_S, st.cuda_stream)
+        rt.check(rc, "sabah_moe_decode")
+
+    # ---- one graph per routing set: x <- x0, then the 48 blocks
+    graphs = []
+    with torch.cuda.stream(stream):
+        for s in range(ROUTING_SETS):        # warm the path once before capture
+            x_d.copy_(x0_d)
+            decode(s, stream)
+        stream.synchronize()
+        for s in range(ROUTING_SETS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                x_d.copy_(x0_d)
+                decode(s, stream)
+            graphs.append(g)
+    stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % ROUTING_SETS].replay()
+    stream.synchronize()
+    clocks = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(args.steps):
+            graphs[i % ROUTING_SETS].replay()
+        t1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # ---- per-kernel device times (eager, same workload, events on the launching stream)
+    timing_steps = 4
+    L.sabah_rt_kernel_timing(1)
+    with torch.cuda.stream(stream):
+        for i in range(timing_steps):
+            x_d.copy_(x0_d)
+            decode(i % ROUTING_SETS, stream)
+    stream.synchronize()
+    buf = ctypes.create_string_buffer(8192)
+    L.sabah_rt_kernel_times(buf, 8192)
+    L.sabah_rt_kernel_timing(0)
+    ktimes = json.loads(buf.value.decode())
+    launches_per_step = sum(v[0] for v in ktimes.values()) / timing_steps
+    # algorithmic bytes per launch of each kernel family
+    kbytes = {
+        "gate_up": TOP_K * 2 * FF * GU_ROW + D_MODEL * 4 + TOP_K * FF * 4,
+        "down": TOP_K * D_MODEL * D_ROW + TOP_K * FF * 4 + 2 * D_MODEL * 4,
+    }
+    dom_name, dom = max(ktimes.items(), key=lambda kv: kv[1][1])
+    family = "gate_up" if "gate_up" in dom_name else "down"
+    avg_ms = dom[1] / dom[0]
+    peaks, peak_kind = measured_peaks()
+    achieved = kbytes[family] / (avg_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": None, "peak_kind": peak_kind, "bytes_per_launch": kbytes[family],
+                "avg_launch_us": round(avg_ms * 1e3, 2),
+                "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)} for k, v in ktimes.items()}}
+
+    # ---- e2e: public C ABI per step, inputs from pinned host memory, result back
+    x0_h = torch.from_numpy(x0()).pin_memory()
+    ids_h = torch.from_numpy(ids_np).pin_memory()
+    w_h = torch.from_numpy(w_np).pin_memory()
+    out_h = torch.empty((1, D_MODEL), dtype=torch.float32).pin_memory()
+    ids_cur = torch.empty_like(ids_d[0])
+    w_cur = torch.empty_like(w_d[0])
+    e2e_steps = max(3, args.steps)
+
+    def e2e_step(s):
+        x_d.copy_(x0_h, non_blocking=True)
+        ids_cur.copy_(ids_h[s], non_blocking=True)
+        w_cur.copy_(w_h[s], non_blocking=True)
+        rc = L.sabah_moe_decode(LAYERS, G, U, D, GU_EXPERT, D_EXPERT, EXPERTS, ids_cur.data_ptr(), w_cur.data_ptr(),
+                                x_d.data_ptr(), h_d.data_ptr(), D_MODEL, FF, TOP_K, 1, QT_IQ3_S, QT_IQ3_S,
+                                QT_IQ3_S, stream.cuda_stream)
+        rt.check(rc, "sabah_moe_decode")
+        out_h.copy_(x_d, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            e2e_step(i % ROUTING_SETS)
+    stream.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            e2e_step(i % ROUTING_SETS)
+        e1.record(stream)
+    stream.synchronize()
+    e_ms = e0.elapsed_time(e1) / e2e_steps
+    e_t = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e_ms = float(e_t.item())
+    assert np.isfinite(out_h.numpy()).all(), "non-finite decode output"
+
+    result = {
+        "metric": METRIC, "value": round(world * 1e3 / ms_max, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (N(0,0.02) weights IQ3_S-encoded on device, N(0,1) router logits)",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+                   "top_k": TOP_K, "weights": "IQ3_S", "tokens_per_step": 1,
+                   "l2": "inputs larger than L2: 973 MB of distinct expert bytes per step, 16 routing sets cycled",
+                   "parallelism": "replicas" if world > 1 else "single"},
+        "achieved_step_gbs": round(BYTES_PER_TOKEN / (ms_max * 1e-3) / 1e9, 1),
+        "roofline": roofline,
+        "e2e": {"value": round(world * 1e3 / e_ms, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x0_h.numel() * 4 + ids_h[0].numel() * 4 + w_h[0].numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
+                "path": "sabah_moe_decode (C ABI), eager launches"},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(bank, gate_p, up_p, down_p, ids_np, w_np, use_ref=False)
+    del graphs
+    return result
+
+
+def _host_sample(bank_ptrs, ids_np, n_layers):
+    """Copy the routed experts of routing set 0 for the first n_layers layers to
+    host memory; returns compact per-layer banks and remapped ids."""
+    from sabah_moe_accelerator_b200 import rt
+    d2h = rt.lib().sabah_memcpy_d2h
+    gate_p, up_p, down_p = bank_ptrs
+    keep = []
+    for Lr in range(n_layers):
+        ids = ids_np[0, Lr, 0]
+        g = np.empty((TOP_K, GU_EXPERT), np.uint8)
+        u = np.empty((TOP_K, GU_EXPERT), np.uint8)
+        d = np.empty((TOP_K, D_EXPERT), np.uint8)
+        for j, e in enumerate(ids):
+            for arr, base, stride in ((g, gate_p[Lr], GU_EXPERT), (u, up_p[Lr], GU_EXPERT), (d, down_p[Lr], D_EXPERT)):
+                rt.check(d2h(arr[j].ctypes.data, base + int(e) * stride, stride), "sample copy")
+        keep.append((g, u, d))
+    return keep
+
+
+def cpu_baseline(bank, gate_p, up_p, down_p, ids_np, w_np, use_ref: bool, n_layers: int = 8):
+    """fp32 CPU decode of the same token (oracle restatement of the reference's
+    CPU path, or the reference's own host dequantizer) on a bounded sample of
+    layers, scaled to the 48-layer token."""
+    from oracle import cpu as orc
+    sample = _host_sample((gate_p, up_p, down_p), ids_np, n_layers)
+    threads = os.cpu_count() or 1
+    local_ids = np.tile(np.arange(TOP_K, dtype=np.int32), (n_layers, 1))
+    x = x0()[0]
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        orc.decode_f32([s[0].ctypes.data for s in sample], [s[1].ctypes.data for s in sample],
+                       [s[2].ctypes.data for s in sample], GU_EXPERT, D_EXPERT, QT_IQ3_S, QT_IQ3_S, local_ids,
+                       w_np[0, :n_layers, 0], x, D_MODEL, FF, threads, use_reference_dequant=use_ref)
+        reps += 1
+        if time.perf_counter() - t0 > 10.0 or reps >= 20:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    per_token = dt * LAYERS / n_layers
+    return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": threads,
+            "kind": "reference" if use_ref else "port",
+            "sample": "%d of 48 blocks of one token (routing set 0), %d repetitions, scaled to 48 blocks" % (
+                n_layers, reps)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's own CPU path (its host dequantizer, compiled
+# from its sources into oracle/_ref) + fp32 dots, all host threads
+# ---------------------------------------------------------------------------
+def run_reference(args, rank: int, world: int, local_rank: int):
+    if rank != 0:
+        return None
+    from oracle import cpu as orc
+    if not orc.ref_available():
+        return {"impl": "reference", "unavailable": "reference build oracle/_ref/libsabah_rt_ref.so is absent"}
+    import torch
+    from sabah_moe_accelerator_b200 import ops
+    torch.cuda.set_device(local_rank)
+    ops.init(local_rank)
+    n_layers = 4
+    # the same inputs as our arm: the routed experts of the first blocks
+    gate_p, up_p, down_p, keep = [], [], [], []
+    for Lr in range(n_layers):
+        for role, rows, k, lst in ((0, FF, D_MODEL, gate_p), (1, FF, D_MODEL, up_p), (2, D_MODEL, FF, down_p)):
+            t = ops.synth_rows(EXPERTS * rows, k, QT_IQ3_S, seed=(10 + Lr) * 4 + role, sigma=0.02)
+            keep.append(t)
+            lst.append(t.data_ptr())
+    torch.cuda.synchronize()
+    ids_np, w_np = routing(1, n_layers)
+    sample = _host_sample((gate_p, up_p, down_p), ids_np, n_layers)
+    del keep
+    threads = os.cpu_count() or 1
+    local_ids = np.tile(np.arange(TOP_K, dtype=np.int32), (n_layers, 1))
+    x = x0()[0]
+
+    def step():
+        orc.decode_f32([s[0].ctypes.data for s in sample], [s[1].ctypes.data for s in sample],
+                       [s[2].ctypes.data for s in sample], GU_EXPERT, D_EXPERT, QT_IQ3_S, QT_IQ3_S, local_ids,
+                       w_np[0, :, 0], x, D_MODEL, FF, threads, use_reference_dequant=True)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    per_token = dt * LAYERS / n_layers
+    v = round(1.0 / per_token, 4)
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_token * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (same inputs as the product arm)",
+            "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+                       "top_k": TOP_K, "weights": "IQ3_S", "tokens_per_step": 1},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                             "sample": "each step: one token through %d of 48 blocks, scaled to 48" % n_layers},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world, local_rank)
+    else:
+        res = run_ours(args, rank, world, local_rank)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,72 @@
+// Internal launch interface between the C-ABI runtime (sb_runtime.cu) and the
+// kernel translation units. Not part of the public ABI.
+#pragma once
+
+#include "sb_common.cuh"
+
+#ifndef SABAH_SENTINEL
+#define SABAH_SENTINEL 0
+#endif
+
+// Where the experts of one call live. Either a pointer table with one expert
+// base per (token, slot) - the hot-tier path - or a device-resident bank that
+// the kernel indexes with the router ids itself (no host round trip).
+struct sb_experts {
+    const void* const* ptrs;       // [n_tokens * n_ids] device pointers, or nullptr
+    const uint8_t* base;           // bank base (used when ptrs == nullptr)
+    size_t expert_stride;          // bytes between experts in the bank
+    const int32_t* ids;            // router ids (used when ptrs == nullptr)
+    size_t ids_id_stride;          // bytes
+    size_t ids_token_stride;       // bytes
+    int n_experts;
+};
+
+// One MUL_MAT_ID call, v2 byte-stride contract.
+struct sb_mmid_args {
+    sb_experts ex;
+    size_t row_stride;
+    const float* x;
+    size_t x_id_stride;
+    int x_rows;
+    size_t x_token_stride;
+    int n_ids, n_tokens;
+    float* dst;
+    size_t dst_id_stride, dst_token_stride;
+    int rows, k, qt;
+    int* err;                      // device-visible error word (host-mapped)
+};
+
+// One fused routed block over n_tokens tokens: gate/up + SwiGLU, then down +
+// top-k weighted combine. Dense fp32 activations:
+//   x [n_tokens][d_model], h [n_tokens][n_used][ff], out [n_tokens][d_model],
+//   w [n_tokens][n_used] routing weights.
+struct sb_block_args {
+    sb_experts gate, up, down;
+    const float* x;
+    float* h;
+    float* out;
+    const float* w;
+    int d_model, ff, n_used, n_tokens;
+    int qt_gate, qt_up, qt_down;
+    int accumulate;                // out += y instead of out = y
+    int* err;
+};
+
+// device-side error codes written to *err
+enum { SB_DERR_NONE = 0, SB_DERR_BAD_ID = 1 };
+
+// Optional per-kernel timing (SABAH_LLAMA_EVENTS=1 or sabah_rt_kernel_timing):
+// launches are bracketed by CUDA events on their own stream and accumulated
+// per kernel name. sb_timing_begin returns a slot id (or -1 when off).
+int sb_timing_begin(const char* name, cudaStream_t st);
+void sb_timing_end(int slot, cudaStream_t st);
+
+int sb_launch_mmid(const sb_mmid_args& a, cudaStream_t st);
+int sb_launch_block(const sb_block_args& a, cudaStream_t st);
+int sb_launch_dequant(const void* src, float* dst, int qt, int n_rows, int row_elems, cudaStream_t st);
+bool sb_qt_supported(int qt);
+
+// fast paths (sb_mmid_iq3s.cu); return 1 if the call was taken, 0 if the
+// shape is not covered (caller falls back), -1 on a launch error
+int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st);
+int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);

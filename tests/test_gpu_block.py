@@ -1,0 +1,87 @@
+"""The fused routed block on the GPU: sabah_moe_block (reference ABI, pointer
+table, one token) and sabah_moe_block_ids (device-resident banks, T tokens),
+against the float64 reference_block (sabah/runtime/executor.py:134-159).
+Reference test: sabah/tests/test_moe_block.py (agreement < 1e-5 rel-L2,
+wrong-expert discrimination).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+TIGHT = 2e-5
+
+
+def _golden_block(golden, bname):
+    p = "block_%s_" % bname
+    return {k: golden[p + k] for k in ("gate", "up", "down", "ids", "w", "x", "want", "types")}
+
+
+@pytest.mark.parametrize("bname", ["iq3s", "q4k_q6k"])
+def test_reference_abi_block_matches_fp64(gpu_rt, orc, golden, bname):
+    from sabah_moe_accelerator_b200 import rt
+    b = _golden_block(golden, bname)
+    qg, qu, qd = [int(v) for v in b["types"]]
+    d_model, ff, n = 256, 256, len(b["ids"])
+    banks = {r: torch.from_numpy(np.ascontiguousarray(b[r]).reshape(-1)).cuda() for r in ("gate", "up", "down")}
+    strides = {r: b[r].shape[1] for r in ("gate", "up", "down")}
+    ptrs = [banks[r].data_ptr() + int(e) * strides[r] for r in ("gate", "up", "down") for e in b["ids"]]
+    d_ptrs = torch.tensor(ptrs, dtype=torch.int64, device="cuda")
+    d_w = torch.from_numpy(b["w"]).cuda()
+    d_x = torch.from_numpy(b["x"]).cuda()
+    d_out = torch.full((d_model,), 7.0, device="cuda")
+    d_h = torch.empty(n * ff, device="cuda")
+    torch.cuda.synchronize()
+    L = gpu_rt
+    rt.check(L.sabah_moe_block(d_x.data_ptr(), d_out.data_ptr(), d_h.data_ptr(), d_ptrs.data_ptr(), d_w.data_ptr(),
+                               d_model, ff, n, qg, qu, qd, 0), "moe_block")
+    rt.check(L.sabah_sync_compute(), "sync")
+    got = d_out.cpu().numpy()
+    r = orc.rel_l2(got, b["want"])
+    assert r <= TOL and r <= TIGHT, r
+    # accumulate: out += y
+    rt.check(L.sabah_moe_block(d_x.data_ptr(), d_out.data_ptr(), d_h.data_ptr(), d_ptrs.data_ptr(), d_w.data_ptr(),
+                               d_model, ff, n, qg, qu, qd, 1), "moe_block acc")
+    rt.check(L.sabah_sync_compute(), "sync")
+    assert orc.rel_l2(d_out.cpu().numpy(), 2 * b["want"]) <= TIGHT
+    # discrimination: one routed expert swapped for another must be far off
+    wrong = [int(e) for e in b["ids"]]
+    wrong[0] = next(e for e in range(b["gate"].shape[0]) if e not in wrong)
+    ptrs = [banks[r].data_ptr() + e * strides[r] for r in ("gate", "up", "down") for e in wrong]
+    d_ptrs.copy_(torch.tensor(ptrs, dtype=torch.int64))
+    torch.cuda.synchronize()
+    rt.check(L.sabah_moe_block(d_x.data_ptr(), d_out.data_ptr(), d_h.data_ptr(), d_ptrs.data_ptr(), d_w.data_ptr(),
+                               d_model, ff, n, qg, qu, qd, 0), "moe_block wrong")
+    rt.check(L.sabah_sync_compute(), "sync")
+    assert orc.rel_l2(d_out.cpu().numpy(), b["want"]) > 100 * TIGHT
+
+
+@pytest.mark.parametrize("qg,qd,T", [(21, 21, 1), (21, 21, 4), (12, 14, 4), (8, 8, 1)])
+def test_block_ids_config_shape(gpu_rt, orc, qg, qd, T):
+    """d_model 2048, ff 768, top-10 of 64 experts, T tokens, banks on the device."""
+    from sabah_moe_accelerator_b200 import ops, rt
+    d_model, ff, E, K = 2048, 768, 64, 10
+    gate = ops.synth_rows(E * ff, d_model, qg, seed=31, sigma=0.02)
+    up = ops.synth_rows(E * ff, d_model, qg, seed=32, sigma=0.02)
+    down = ops.synth_rows(E * d_model, ff, qd, seed=33, sigma=0.02)
+    rng = np.random.default_rng(T)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, K)).astype(np.float32)
+    w /= w.sum(1, keepdims=True)
+    x = rng.standard_normal((T, d_model)).astype(np.float32)
+    out = ops.moe_block_ids(gate, up, down, torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(),
+                            torch.from_numpy(x).cuda(), d_model, ff, E, qg, qg, qd)
+    got = out.cpu().numpy()
+    g, u, d = gate.cpu().numpy(), up.cpu().numpy(), down.cpu().numpy()
+    for t in range(T):
+        want = orc.moe_block_f64(g.reshape(E, -1), u.reshape(E, -1), d.reshape(E, -1), ids[t], w[t], x[t],
+                                 d_model, ff, qg, qg, qd)
+        r = orc.rel_l2(got[t], want)
+        assert r <= TOL and r <= TIGHT, (t, r)
+    del rt, ctypes

@@ -53,7 +53,7 @@ struct sb_block_args {
 };
 
 // device-side error codes written to *err
-enum { SB_DERR_NONE = 0, SB_DERR_BAD_ID = 1 };
+enum { SB_DERR_NONE = 0, SB_DERR_BAD_ID = 1, SB_DERR_TIMEOUT = 2, SB_DERR_MISALIGNED = 3 };
 
 // Optional per-kernel timing (SABAH_LLAMA_EVENTS=1 or sabah_rt_kernel_timing):
 // launches are bracketed by CUDA events on their own stream and accumulated

@@ -63,11 +63,6 @@ bool sb_cuda_ok(cudaError_t e, const char* what) {
 // ---------------------------------------------------------------------------
 // configuration (environment variables, same names as the reference)
 // ---------------------------------------------------------------------------
-static bool env_on(const char* name) {
-    const char* v = std::getenv(name);
-    return v && *v && *v != '0';
-}
-
 // "9800000000", "9.8e9", "9.8G", "9800MiB"; a value that does not parse whole
 // is refused (ref sabah_rt.cu:276-330 explains the 9.8e9 -> 9 bytes failure).
 static bool parse_size(const char* text, size_t& out) {
@@ -157,8 +152,11 @@ struct Slab {
         reset_lists();
     }
     // best fit: the smallest free range that holds the request, lowest offset on ties
+    // sizes are rounded up to 256 B so every range starts 256-byte aligned
+    // (the bulk-copy kernels need 16-byte aligned expert bases)
     void* alloc_locked(size_t bytes) {
-        if (!base || bytes == 0) return nullptr;
+        if (!base || bytes == 0 || bytes > ((size_t)1 << 60)) return nullptr;
+        bytes = (bytes + 255) & ~(size_t)255;
         auto it = free_by_len.lower_bound({bytes, 0});
         if (it == free_by_len.end()) return nullptr;
         const size_t len = it->first, off = it->second;
@@ -172,7 +170,6 @@ struct Slab {
         live[p] = bytes;
         return p;
     }
-    bool owns(void* p) const { return base && (char*)p >= base && (char*)p < base + size; }
     void free_locked(void* p) {
         auto it = live.find(p);
         if (it == live.end()) return;
@@ -497,8 +494,10 @@ bool device_errors_clear() {
     if (g_rt.err_h && *(volatile int*)g_rt.err_h != SB_DERR_NONE) {
         const int code = *(volatile int*)g_rt.err_h;
         *(volatile int*)g_rt.err_h = SB_DERR_NONE;
-        sb_set_error("a kernel found an expert id outside [0, n_experts) (device error %d, reported by the "
-                     "first call after it ran)", code);
+        sb_set_error("%s (device error %d, reported by the first call after the kernel ran)",
+                     code == SB_DERR_BAD_ID ? "a kernel found an expert id outside [0, n_experts)"
+                     : code == SB_DERR_MISALIGNED ? "an expert base was not 16-byte aligned"
+                     : "a kernel gave up waiting for its weight tiles", code);
         return false;
     }
     return true;
@@ -689,8 +688,10 @@ SABAH_API const char* sabah_rt_last_error(void) { return g_err; }
 SABAH_API int sabah_rt_init(int device) {
     if (!sb_cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return -1;
     if (!g_rt.copy) {
-        SB_CUDA(cudaStreamCreateWithFlags(&g_rt.copy, cudaStreamNonBlocking), "create copy stream");
-        SB_CUDA(cudaStreamCreateWithFlags(&g_rt.compute, cudaStreamNonBlocking), "create compute stream");
+        // blocking streams, as the reference creates them: work a caller queued
+        // on the legacy default stream is ordered before anything issued here
+        SB_CUDA(cudaStreamCreate(&g_rt.copy), "create copy stream");
+        SB_CUDA(cudaStreamCreate(&g_rt.compute), "create compute stream");
     }
     if (!g_rt.err_h) {
         SB_CUDA(cudaHostAlloc((void**)&g_rt.err_h, sizeof(int), cudaHostAllocMapped), "error word");

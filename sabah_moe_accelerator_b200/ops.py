@@ -24,8 +24,11 @@ def init(device: int = 0) -> None:
 
 
 def _stream(stream) -> int:
+    """Raw stream handle for the C ABI. torch's default stream has handle 0,
+    which the ABI reads as "the runtime's own stream"; it is passed as the
+    explicit legacy-stream handle (cudaStreamLegacy = 1) instead."""
     s = stream if stream is not None else torch.cuda.current_stream()
-    return s.cuda_stream
+    return s.cuda_stream or 1
 
 
 def _ptr(t) -> int:

@@ -84,4 +84,3 @@ def test_block_ids_config_shape(gpu_rt, orc, qg, qd, T):
                                  d_model, ff, qg, qg, qd)
         r = orc.rel_l2(got[t], want)
         assert r <= TOL and r <= TIGHT, (t, r)
-    del rt, ctypes

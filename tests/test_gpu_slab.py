@@ -81,11 +81,14 @@ def test_copy_wait_event_contract(gpu_rt):
 
 def test_pinned_pool_reuses_blocks(gpu_rt):
     L = gpu_rt
-    a = L.sabah_host_alloc(1 << 16)
+    a = L.sabah_host_alloc(1 << 22)
     L.sabah_host_free(a)
-    b = L.sabah_host_alloc(1 << 12)
+    b = L.sabah_host_alloc(1 << 22)     # the freed 4 MiB block is handed out again
     assert a == b
+    c = L.sabah_host_alloc(1 << 22)     # while b is live, a second request gets a new block
+    assert c != b
     L.sabah_host_free(b)
+    L.sabah_host_free(c)
 
 
 def test_dev_mem_reports_a_b200_sized_device(gpu_rt):

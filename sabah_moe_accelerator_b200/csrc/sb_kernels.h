@@ -70,3 +70,6 @@ bool sb_qt_supported(int qt);
 // shape is not covered (caller falls back), -1 on a launch error
 int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st);
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);
+// After a device error: the fused block's cross-CTA arrival counters may have
+// been left mid-count by a kernel that gave up; the next call clears them.
+void sb_block_scratch_invalidate();

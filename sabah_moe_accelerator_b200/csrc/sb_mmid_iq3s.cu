@@ -40,6 +40,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <utility>
 
 #include "sb_kernels.h"
 #include "sb_quant.cuh"
@@ -50,41 +51,49 @@ constexpr int kConsumers = 12;                   // consumer warps
 constexpr int kThreads = (kConsumers + 1) * 32;  // + one producer warp
 constexpr int kReplicas = 16;
 constexpr int kTableBytes = 512 * kReplicas * 4; // 32 KB
-constexpr int kStageBytes = 14336;               // >= 16 rows x 880 B
-constexpr int kStages = 9;
+// Tile ring: kRingBytes of shared memory cut into n_stages stages of one
+// 16-row tile each (8 x 14,080 B for k = 2048, 24 x 5,280 B for k = 768).
+// A lane issues its bulk copies one after another (~0.34 us apiece), so
+// kIssuers producer lanes each own every kIssuers-th stage; n_stages is a
+// multiple of kIssuers, so a stage always belongs to the same lane and its
+// mbarrier phases are waited on in order.
+constexpr int kRingBytes = 9 * 14336;
+constexpr int kMaxStages = 24;
+constexpr int kIssuers = 8;
+constexpr int kMaxTileBytes = 16 * 880;
 constexpr int kSets = 4;
 constexpr int kRecBytes = 72;                    // per (group, step): 4 quads x (hi, lo) x 8 B + 8 B zeros
 constexpr int kGroupBytes = 8 * kRecBytes + 16;  // 8 records + 4 per-sub-block inverse scales
 constexpr int kSetBytes = 16 * kGroupBytes;      // k <= 2048
 constexpr int kMaxWpt = 4;
 constexpr int kMaxP = 4;                         // items in flight (kConsumers / wpt, wpt >= 3)
-// Reduction slots: each in-flight position owns a ring of kRing slots. Warps of
-// one position take its items in order, and a warp can run at most
-// kStages / (ntile * P) <= 3 of the position's items ahead of the slowest one
-// (the stage ring holds it back), so a ring of 4 is never overwritten while
-// the last warp of an older item still reads it.
-constexpr int kRing = 4;
-constexpr int kRedSlots = kMaxP * kRing;
-constexpr long long kSpinLimit = 1ll << 26;      // bounded waits
+// The wpt warps of an item leave their partial rows in the item's stage slot of
+// `red` and count themselves in; the last one reads them, runs the epilogue and
+// only then releases the stage, so a slot is never reused while it is read.
+constexpr int kRedSlots = kMaxStages;
+constexpr int kSuspendNs = 20000;                // try_wait suspend hint
+constexpr long long kSpinLimit = 1ll << 17;      // bounded waits: <= 2^17 x 20 us ~ 2.6 s
 
 enum Mode { MODE_MMID = 0, MODE_GATE_UP = 1, MODE_DOWN = 2 };
 
 struct Desc {
+    int seq;       // sequence number of the tile in the stage (see the consumer wait)
     int bad;       // 0 valid, else the device error code (the epilogue emits NaN)
     int slot;      // x-fragment set
     int t, e, rt;  // token, slot (expert choice), row tile
+    int which;     // gate/up: 0 gate, 1 up
 };
 
 struct Smem {
     static constexpr int table = 0;
     static constexpr int stages = table + kTableBytes;
-    static constexpr int sets = stages + kStages * kStageBytes;
-    static constexpr int red = sets + kSets * kSetBytes;                  // [kRedSlots][kMaxWpt][32] floats
-    static constexpr int desc = red + kRedSlots * kMaxWpt * 32 * 4;      // [kStages] Desc
-    static constexpr int cnt = desc + kStages * (int)sizeof(Desc);       // [kRedSlots] ints
+    static constexpr int sets = stages + kRingBytes;
+    static constexpr int red = sets + kSets * kSetBytes;                  // [kRedSlots][kMaxWpt][16] floats
+    static constexpr int desc = red + kRedSlots * kMaxWpt * 16 * 4;      // [kMaxStages] Desc
+    static constexpr int cnt = desc + kMaxStages * (int)sizeof(Desc);    // [kRedSlots] ints
     static constexpr int abort_flag = cnt + kRedSlots * 4;
-    static constexpr int bars = (abort_flag + 4 + 7) & ~7;                // full[kStages], empty[kStages]
-    static constexpr int total = bars + 2 * kStages * 8;
+    static constexpr int bars = (abort_flag + 4 + 7) & ~7;                // full[kMaxStages], empty[kMaxStages]
+    static constexpr int total = bars + 2 * kMaxStages * 8;
 };
 static_assert(Smem::total <= 227 * 1024, "shared memory budget");
 
@@ -94,10 +103,12 @@ struct Params {
     int per_key;           // consecutive items sharing one x vector
     int wpt, gpw, P;       // warps per item, groups per warp, items in flight (12 / wpt)
     int k, rb, rtiles;     // row length, row bytes, 16-row tiles per matrix
+    int n_stages;          // ring stages (multiple of kIssuers, <= kMaxStages)
+    int stage_bytes;       // 16 * rb rounded up to 128
     sb_mmid_args m;
     sb_block_args b;
-    float* partial;        // DOWN: [T][n_used][d_model]
-    int* counters;         // DOWN: [T][d_model / 16], self-resetting
+    float* partial;        // DOWN: [T][n_used][d_model]; GATE_UP: [T][n_used][2][ff]
+    int* counters;         // DOWN: [T][d_model / 16]; GATE_UP: [T][n_used][ff / 16]; self-resetting
     int* err;
 };
 
@@ -113,12 +124,15 @@ __device__ inline void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ inline void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (up to the hint) instead of spinning, so waiting producer lanes and
+// consumers do not steal issue slots from the warps that are decoding
 __device__ inline bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "n"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -128,7 +142,19 @@ __device__ inline bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ inline bool mbar_wait(uint32_t bar, uint32_t parity, int* err, volatile int* abort_flag) {
     for (long long i = 0; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 255 && *abort_flag) return false;
+        if ((i & 15) == 15 && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    if (err) atomicExch(err, SB_DERR_TIMEOUT);
+    return false;
+}
+// Bounded wait for the producer's sequence stamp on a stage descriptor.
+__device__ inline bool wait_seq(const int* stamp, int seq, int* err, volatile int* abort_flag) {
+    const volatile int* v = stamp;
+    for (long long i = 0; i < kSpinLimit * 64; ++i) {
+        if (*v == seq) return true;
+        if (*abort_flag) return false;
+        __nanosleep(64);
     }
     *abort_flag = 1;
     if (err) atomicExch(err, SB_DERR_TIMEOUT);
@@ -154,7 +180,38 @@ __device__ inline void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ inline uint32_t lds_u16(const uint8_t* p) { return *(const unsigned short*)p; }
+// shared-memory loads at 32-bit addresses with a compile-time offset (keeps the
+// address arithmetic out of the decode loop)
+template <int OFF>
+__device__ inline uint32_t ld_u8(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u8 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ inline uint32_t ld_u16(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u16 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ inline uint32_t ld_u32(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ inline uint2 ld_v2(uint32_t a) {
+    uint2 v;
+    asm("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(a), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ inline float ld_f32(uint32_t a) {
+    float v;
+    asm("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(a), "n"(OFF));
+    return v;
+}
 
 // ---------------------------------------------------------------- items
 __device__ inline const uint8_t* expert_ptr(const sb_experts& ex, int t, int i, int n_ids) {
@@ -167,9 +224,15 @@ __device__ inline const uint8_t* expert_ptr(const sb_experts& ex, int t, int i, 
     return ex.base + (size_t)id * ex.expert_stride;
 }
 
-// 16-row tile `which` (0, or 1 = up for gate/up) of item `item`, its token/slot/row tile
-__device__ inline const uint8_t* item_tile(const Params& p, int item, int which, int& t, int& e, int& rt) {
+// The 16-row tile of item `item`, its token / slot / row tile. Gate/up items
+// alternate gate (even) and up (odd) tiles of the same rows.
+__device__ inline const uint8_t* item_tile(const Params& p, int item, int& which, int& t, int& e, int& rt) {
     const int rtiles = p.rtiles;
+    which = 0;
+    if (p.mode == MODE_GATE_UP) {
+        which = item & 1;
+        item >>= 1;
+    }
     rt = item % rtiles;
     const int si = item / rtiles;
     const uint8_t* base;
@@ -244,72 +307,99 @@ __device__ void build_set(const float* x, int k, uint8_t* set) {
 }
 
 // ---------------------------------------------------------------- decode core
-// Decode groups [q0, q0 + NG) of a 16-row tile (NG interleaved MMA chains) and
-// add their sub-block dots into acc[0] (row g) and acc[1] (row g + 8).
-template <int NG>
-__device__ inline void do_groups(const uint8_t* tile, int rb, int q0, const uint8_t* set, int boff,
-                                 const uint32_t* table_lane, int g, int c, float (&acc)[2]) {
-    uint32_t qs[NG][2][4], qh[NG][2], sgw[NG][2][4];
-    float db[NG][2];
+// Per-thread constant addresses (32-bit shared-memory addresses).
+struct Lane {
+    uint32_t table;    // replica (lane % 16) of the grid table
+    uint32_t invd;     // from a lane's B record to its quad's inverse scale: 4c - boff (mod 2^32)
+    uint32_t row8c;    // tile-relative offsets of row g: + 8c (qs), + 4c (signs), + c (qh), + c/2 (scales)
+    uint32_t row4c, row1c, rowhc, row0;
+    uint32_t rb8;      // 8 rows
+    int nib_shift;     // 4 * (c & 1): the scale nibble of sub-block 4n + c
+};
+
+// Per-(row, sub-block) fields of group N of a pair (N = 0: sub-block c of the
+// super-block, N = 1: sub-block 4 + c): the 8 qs bytes (4 u16), the 4 sign
+// bytes, the qh byte spread to one 0/1 byte per entry (the 9th index bit), and
+// the sub-block scale db = d * (1 + 2 * nibble) * (x inverse scale).
+template <int N>
+__device__ inline void load_fields(uint32_t r8, uint32_t r4, uint32_t r1, uint32_t rh, uint32_t invq, int nib_shift,
+                                   float d, uint32_t (&qsw)[4], uint32_t (&QH)[2], uint32_t (&sgw)[4], float& db) {
+    qsw[0] = ld_u16<2 + 32 * N>(r8);
+    qsw[1] = ld_u16<4 + 32 * N>(r8);
+    qsw[2] = ld_u16<6 + 32 * N>(r8);
+    qsw[3] = ld_u16<8 + 32 * N>(r8);
+    sgw[0] = ld_u8<74 + 16 * N>(r4);
+    sgw[1] = ld_u8<75 + 16 * N>(r4);
+    sgw[2] = ld_u8<76 + 16 * N>(r4);
+    sgw[3] = ld_u8<77 + 16 * N>(r4);
+    const uint32_t qh = ld_u8<66 + 4 * N>(r1);
+    QH[0] = ((qh & 15u) * 0x00204081u) & 0x01010101u;   // qh bits 0..3 -> bytes 0..3
+    QH[1] = ((qh >> 4) * 0x00204081u) & 0x01010101u;    // qh bits 4..7 -> bytes 0..3
+    const uint32_t nib = (ld_u8<106 + 2 * N>(rh) >> nib_shift) & 15u;
+    const float inv = ld_f32<N * kGroupBytes + 8 * kRecBytes>(invq);
+    db = d * (float)(1 + 2 * (int)nib) * inv;
+}
+
+// Step S (grid entry S of every sub-block) of both groups of a pair: decode
+// rows g and g + 8 of entry S into A fragments and issue the two MMAs.
+template <int S>
+__device__ inline void step(uint32_t setq, uint32_t table, const uint32_t (&qsw)[2][2][4], const uint32_t (&QH)[2][2][2],
+                            const uint32_t (&sgw)[2][2][4], float (&dd)[2][4]) {
+    // PRMT selector: byte 0 = qs byte (S & 1) of the u16 word, byte 1 = QH byte (S & 3), bytes 2, 3 = 0
+    constexpr uint32_t sel = (uint32_t)(S & 1) | ((4u + (S & 3)) << 4) | (2u << 8) | (2u << 12);
+    constexpr uint32_t mask = (S & 1) ? 0xF0u : 0x0Fu;                 // entry S's sign nibble
+    constexpr uint32_t kspread = (S & 1) ? 0x01020408u : 0x10204080u;  // nibble bits -> bit 7 of bytes 0..3
+    const uint2 bv[2] = {ld_v2<S * kRecBytes>(setq), ld_v2<kGroupBytes + S * kRecBytes>(setq)};
 #pragma unroll
-    for (int n = 0; n < NG; ++n) {
-        const int q = q0 + n;
-        const int jj = 4 * (q & 1) + c;   // sub-block inside the super-block
-        const float inv = ((const float*)(set + q * kGroupBytes + 8 * kRecBytes))[c];
+    for (int n = 0; n < 2; ++n) {
+        uint32_t a[2][2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const uint8_t* bp = tile + (g + 8 * h) * rb + (q >> 1) * 110;
-            const uint8_t* q8 = bp + 2 + 8 * jj;
-#pragma unroll
-            for (int w = 0; w < 4; ++w) qs[n][h][w] = lds_u16(q8 + 2 * w);
-            qh[n][h] = (uint32_t)bp[66 + jj] << 8;
-            const uint32_t sg = lds_u16(bp + 74 + 4 * jj) | (lds_u16(bp + 76 + 4 * jj) << 16);
-            // sign nibble of entry s sits in the low or high nibble of sgw[s / 2]
-            sgw[n][h][0] = sg;
-            sgw[n][h][1] = sg >> 8;
-            sgw[n][h][2] = sg >> 16;
-            sgw[n][h][3] = sg >> 24;
-            const int nib = (bp[106 + (jj >> 1)] >> (4 * (jj & 1))) & 15;
-            db[n][h] = __half2float(__ushort_as_half((unsigned short)lds_u16(bp))) * (float)(1 + 2 * nib) * inv;
+            const uint32_t idx = prmt(qsw[n][h][S >> 1], QH[n][h][S >> 2], sel);
+            uint32_t grid;
+            asm("ld.shared.u32 %0, [%1];" : "=r"(grid) : "r"((idx << 6) + table));
+            const uint32_t Z = ((sgw[n][h][S >> 1] & mask) * kspread) & 0x80808080u;
+            a[h][0] = prmt(grid, Z, 0x5140);   // (e0, e1) as signed fp16 subnormals
+            a[h][1] = prmt(grid, Z, 0x7362);   // (e2, e3)
         }
-    }
-    float d[NG][4];
-#pragma unroll
-    for (int n = 0; n < NG; ++n) d[n][0] = d[n][1] = d[n][2] = d[n][3] = 0.f;
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-#pragma unroll
-        for (int n = 0; n < NG; ++n) {
-            const uint2 bv = *(const uint2*)(set + (q0 + n) * kGroupBytes + s * kRecBytes + boff);
-            uint32_t a[2][2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t w = qs[n][h][s >> 1];
-                const uint32_t qsb = (s & 1) ? (w >> 8) : (w & 0xffu);
-                const uint32_t idx = qsb | ((qh[n][h] >> s) & 0x100u);
-                const uint32_t grid = table_lane[idx * kReplicas];
-                // the 4 sign bits -> bit 7 of bytes 0..3 (nibble at bit 0 or 4 of sgw)
-                const uint32_t nib = sgw[n][h][s >> 1] & ((s & 1) ? 0xF0u : 0x0Fu);
-                const uint32_t Z = (nib * ((s & 1) ? 0x01020408u : 0x10204080u)) & 0x80808080u;
-                a[h][0] = prmt(grid, Z, 0x5140);   // (e0, e1) as signed fp16 subnormals
-                a[h][1] = prmt(grid, Z, 0x7362);   // (e2, e3)
-            }
-            mma16816(d[n], a[0][0], a[1][0], a[0][1], a[1][1], bv.x, bv.y);
-        }
-    }
-#pragma unroll
-    for (int n = 0; n < NG; ++n) {
-        acc[0] = fmaf(db[n][0], d[n][0] + d[n][1], acc[0]);
-        acc[1] = fmaf(db[n][1], d[n][2] + d[n][3], acc[1]);
+        mma16816(dd[n], a[0][0], a[1][0], a[0][1], a[1][1], bv[n].x, bv[n].y);
     }
 }
 
-__device__ inline void decode_tile(const uint8_t* tile, int rb, int q0, int gpw, const uint8_t* set, int boff,
-                                   const uint32_t* table_lane, int g, int c, float (&acc)[2]) {
-    int q = q0;
-    const int qe = q0 + gpw;
-    for (; q + 2 <= qe; q += 2) do_groups<2>(tile, rb, q, set, boff, table_lane, g, c, acc);
-    if (q < qe) do_groups<1>(tile, rb, q, set, boff, table_lane, g, c, acc);
+template <int... S>
+__device__ inline void all_steps(std::integer_sequence<int, S...>, uint32_t setq, uint32_t table,
+                                 const uint32_t (&qsw)[2][2][4], const uint32_t (&QH)[2][2][2],
+                                 const uint32_t (&sgw)[2][2][4], float (&dd)[2][4]) {
+    (step<S>(setq, table, qsw, QH, sgw, dd), ...);
+}
+
+// Decode the group pair (q, q + 1), q even (the two halves of super-block q / 2),
+// of a 16-row tile at shared address tile: 2 interleaved MMA chains; adds the
+// sub-block dots of rows g and g + 8 into acc[0] and acc[1]. setB = x-set base
+// + this lane's B-record offset.
+__device__ inline void do_pair(uint32_t tile, int q, uint32_t setB, const Lane& L, float (&acc)[2]) {
+    const uint32_t sb = tile + (uint32_t)(q >> 1) * 110u;
+    const uint32_t setq = setB + (uint32_t)q * kGroupBytes;
+    const uint32_t invq = setq + L.invd;
+    uint32_t qsw[2][2][4], QH[2][2][2], sgw[2][2][4];
+    float db[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t r8 = sb + L.row8c + h * L.rb8, r4 = sb + L.row4c + h * L.rb8;
+        const uint32_t r1 = sb + L.row1c + h * L.rb8, rh = sb + L.rowhc + h * L.rb8;
+        const float d = __half2float(__ushort_as_half((unsigned short)ld_u16<0>(sb + L.row0 + h * L.rb8)));
+        load_fields<0>(r8, r4, r1, rh, invq, L.nib_shift, d, qsw[0][h], QH[0][h], sgw[0][h], db[0][h]);
+        load_fields<1>(r8, r4, r1, rh, invq, L.nib_shift, d, qsw[1][h], QH[1][h], sgw[1][h], db[1][h]);
+    }
+    float dd[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) dd[n][0] = dd[n][1] = dd[n][2] = dd[n][3] = 0.f;
+    all_steps(std::make_integer_sequence<int, 8>{}, setq, L.table, qsw, QH, sgw, dd);
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        acc[0] = fmaf(db[n][0], dd[n][0] + dd[n][1], acc[0]);
+        acc[1] = fmaf(db[n][1], dd[n][2] + dd[n][3], acc[1]);
+    }
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -317,10 +407,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* bars = (uint64_t*)(smem + Smem::bars);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kMaxStages);
+    const int ns = p.n_stages;
     volatile int* abort_flag = (volatile int*)(smem + Smem::abort_flag);
     Desc* descs = (Desc*)(smem + Smem::desc);
-    const int ntile = p.mode == MODE_GATE_UP ? 2 : 1;   // tiles (stages) per item
 
     // let the next kernel on the stream begin its prologue as SMs free up
     asm volatile("griddepcontrol.launch_dependents;");
@@ -331,44 +421,49 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
 
     if (threadIdx.x == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < ns; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, p.wpt);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x < kRedSlots) ((int*)(smem + Smem::cnt))[threadIdx.x] = 0;
+    if (threadIdx.x < kMaxStages) descs[threadIdx.x].seq = -1;
     __syncthreads();
 
     if (warp == kConsumers) {
         // ------------------------------------------------------ producer
-        if (lane == 0) {
+        // lane l issues sequence numbers n = l, l + kIssuers, ... (stage n % ns,
+        // always the same lane for a given stage); each lane looks up its own
+        // tiles' expert addresses, so those loads overlap across lanes
+        if (lane < kIssuers) {
             const uint32_t st0 = smem_u32(smem + Smem::stages);
             const uint32_t bytes = 16u * p.rb;
-            int issued = 0;
-            for (int item = i0; item < i1 && !*abort_flag; ++item) {
-                for (int w = 0; w < ntile; ++w, ++issued) {
-                    const int s = issued % kStages;
-                    if (issued >= kStages &&
-                        !mbar_wait(empty0 + 8 * s, ((issued / kStages) - 1) & 1, p.err, abort_flag))
-                        break;
-                    Desc d;
-                    const uint8_t* src = item_tile(p, item, w, d.t, d.e, d.rt);
-                    d.bad = !src ? SB_DERR_BAD_ID : ((uintptr_t)src & 15) ? SB_DERR_MISALIGNED : 0;
-                    d.slot = (item / p.per_key) % kSets;
-                    descs[s] = d;   // published by the arrive below (release)
-                    if (!d.bad) {
-                        mbar_expect_tx(full0 + 8 * s, bytes);
-                        bulk_g2s(st0 + s * kStageBytes, src, bytes, full0 + 8 * s);
-                    } else {
-                        mbar_arrive(full0 + 8 * s);
-                    }
+            int last = -1;
+            for (int n = lane; i0 + n < i1 && !*abort_flag; n += kIssuers) {
+                const int s = n % ns;
+                if (n >= ns && !mbar_wait(empty0 + 8 * s, ((n / ns) - 1) & 1, p.err, abort_flag)) break;
+                const int item = i0 + n;
+                Desc d;
+                const uint8_t* src = item_tile(p, item, d.which, d.t, d.e, d.rt);
+                d.bad = !src ? SB_DERR_BAD_ID : ((uintptr_t)src & 15) ? SB_DERR_MISALIGNED : 0;
+                d.slot = (item / p.per_key) % kSets;
+                d.seq = -1;
+                descs[s] = d;   // published by the arrive below (release)
+                __threadfence_block();
+                *(volatile int*)&descs[s].seq = n;   // the stage's previous tile is released
+                if (!d.bad) {
+                    mbar_expect_tx(full0 + 8 * s, bytes);
+                    bulk_g2s(st0 + s * p.stage_bytes, src, bytes, full0 + 8 * s);
+                } else {
+                    mbar_arrive(full0 + 8 * s);
                 }
+                last = n;
             }
-            // never leave with copies in flight: the last use of every stage must land
-            for (int n = std::max(0, issued - kStages); n < issued; ++n)
-                for (long long i = 0; i < kSpinLimit && !mbar_try_wait(full0 + 8 * (n % kStages), (n / kStages) & 1);
-                     ++i) {
+            // never leave with copies in flight: the last use of each of this
+            // lane's stages must have landed
+            for (int n = std::max(lane, last - ns + kIssuers); n <= last; n += kIssuers)
+                for (long long i = 0; i < kSpinLimit && !mbar_try_wait(full0 + 8 * (n % ns), (n / ns) & 1); ++i) {
                 }
         }
         return;
@@ -387,13 +482,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int g = lane >> 2, c = lane & 3;
-    const uint32_t* table_lane = table + (lane & (kReplicas - 1));
     const int boff = (g >> 1) == c ? (2 * c + (g & 1)) * 8 : 64;
+    Lane L;
+    L.table = smem_u32(table) + (lane & (kReplicas - 1)) * 4;
+    L.invd = (uint32_t)(4 * c - boff);
+    L.row0 = (uint32_t)(g * p.rb);
+    L.row8c = L.row0 + 8 * c;
+    L.row4c = L.row0 + 4 * c;
+    L.row1c = L.row0 + c;
+    L.rowhc = L.row0 + (c >> 1);
+    L.rb8 = (uint32_t)(8 * p.rb);
+    L.nib_shift = 4 * (c & 1);
+    const uint32_t stages32 = smem_u32(smem + Smem::stages), sets32 = smem_u32(smem + Smem::sets);
     const int pos = warp / p.wpt;   // which of the P items in flight
     const int wsub = warp % p.wpt;  // which part of the row
     float* red = (float*)(smem + Smem::red);
     int* cnt = (int*)(smem + Smem::cnt);
-    const uint8_t* stages = smem + Smem::stages;
     uint8_t* sets = smem + Smem::sets;
 
     // Items are walked in chunks whose x vectors map to distinct set slots
@@ -410,61 +514,56 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
                 build_set(key_vector(p, key), p.k, sets + (key % kSets) * kSetBytes);
         }
         consumers_sync();
-        for (int it = item + pos, j = 0; it < chunk_end; it += p.P, ++j) {
-            const int n_local = it - i0;               // item index in this CTA's sequence
-            const int rslot = pos * kRing + (j % kRing);
-            float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-            Desc d{};
-            int bad = 0;
-            for (int w = 0; w < ntile; ++w) {
-                const int seq = n_local * ntile + w;    // stage sequence number
-                const int s = seq % kStages;
-                const bool landed = mbar_wait(full0 + 8 * s, (seq / kStages) & 1, p.err, abort_flag);
-                d = descs[s];
-                if (landed && !d.bad)
-                    decode_tile(stages + s * kStageBytes, p.rb, wsub * p.gpw, p.gpw, sets + d.slot * kSetBytes, boff,
-                                table_lane, g, c, acc[w]);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty0 + 8 * s);
-                if (!bad) bad = landed ? d.bad : SB_DERR_TIMEOUT;
-            }
-            d.bad = bad;
+        for (int it = item + pos; it < chunk_end; it += p.P) {
+            const int seq = it - i0;   // one stage per item, in this CTA's order
+            const int s = seq % ns;
+            // The producer stamps seq into the stage descriptor only after the
+            // stage's previous tile (seq - ns) was released, so once the stamp is
+            // seen the parity wait refers to this tile's phase. Without it, a warp
+            // running ns tiles ahead of a late copy would take the old phase's
+            // completion for its own.
+            const bool stamped = wait_seq(&descs[s].seq, seq, p.err, abort_flag);
+            const bool landed = stamped && mbar_wait(full0 + 8 * s, (seq / ns) & 1, p.err, abort_flag);
+            const Desc d = descs[s];
+            const int bad = !stamped ? -1 : !landed ? SB_DERR_TIMEOUT : d.bad;
+            float acc[2] = {0.f, 0.f};
+            if (!bad)
+                for (int q = wsub * p.gpw; q < (wsub + 1) * p.gpw; q += 2)
+                    do_pair(stages32 + s * p.stage_bytes, q, sets32 + d.slot * kSetBytes + boff, L, acc);
             // this warp's rows: reduce the 4 quads, publish, count
 #pragma unroll
-            for (int w = 0; w < 2; ++w)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    acc[w][h] += __shfl_xor_sync(0xffffffffu, acc[w][h], 1);
-                    acc[w][h] += __shfl_xor_sync(0xffffffffu, acc[w][h], 2);
-                }
-            float* rr = red + (rslot * kMaxWpt + wsub) * 32;
+            for (int h = 0; h < 2; ++h) {
+                acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+                acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
+            }
+            float* rr = red + (s * kMaxWpt + wsub) * 16;
             if (c == 0) {
-                rr[g] = acc[0][0];
-                rr[g + 8] = acc[0][1];
-                rr[16 + g] = acc[1][0];
-                rr[16 + g + 8] = acc[1][1];
+                rr[g] = acc[0];
+                rr[g + 8] = acc[1];
             }
             __threadfence_block();
             __syncwarp();
             int last = 0;
             if (lane == 0) {
-                last = atomicAdd(cnt + rslot, 1) == p.wpt - 1;
-                if (last) cnt[rslot] = 0;
+                last = atomicAdd(cnt + s, 1) == p.wpt - 1;
+                if (last) cnt[s] = 0;
+                else mbar_arrive(empty0 + 8 * s);
             }
             last = __shfl_sync(0xffffffffu, last, 0);
             if (!last) continue;
-            __threadfence_block();
             // ---- epilogue (the last warp of the item), one row per lane
+            __threadfence_block();
+            float v = 0.f;
+            if (lane < 16)
+                for (int w = 0; w < p.wpt; ++w) v += red[(s * kMaxWpt + w) * 16 + lane];
+            __syncwarp();
+            // the partial rows are read: the stage (and its red slot) may be reused
+            if (lane == 0) mbar_arrive(empty0 + 8 * s);
+            if (bad < 0) continue;   // no descriptor (the CTA is aborting; the error is recorded)
             if (lane < 16) {
-                const float* r0 = red + rslot * kMaxWpt * 32;
-                float v = 0.f, u = 0.f;
-                for (int w = 0; w < p.wpt; ++w) {
-                    v += r0[w * 32 + lane];
-                    u += r0[w * 32 + 16 + lane];
-                }
-                if (d.bad) {
-                    v = u = __int_as_float(0x7fc00000);
-                    if (lane == 0 && p.err) atomicExch(p.err, d.bad);
+                if (bad) {
+                    v = __int_as_float(0x7fc00000);
+                    if (lane == 0 && p.err) atomicExch(p.err, bad);
                 }
                 const int row = d.rt * 16 + lane;
                 if (p.mode == MODE_MMID) {
@@ -472,7 +571,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
                                           (size_t)d.e * p.m.dst_id_stride);
                     dst[row] = v;
                 } else if (p.mode == MODE_GATE_UP) {
-                    p.b.h[((size_t)d.t * p.b.n_used + d.e) * p.b.ff + row] = v / (1.f + expf(-v)) * u;
+                    // gate and up of these rows may be decoded by different CTAs: each
+                    // writes its half, the second to finish forms silu(g) * u
+                    const size_t te = (size_t)d.t * p.b.n_used + d.e;
+                    p.partial[(te * 2 + d.which) * p.b.ff + row] = v;
+                    __threadfence();
+                    __syncwarp(0x0000ffffu);
+                    int fin = 0;
+                    if (lane == 0) {
+                        int* gc = p.counters + te * p.rtiles + d.rt;
+                        fin = atomicAdd(gc, 1) == 1;
+                        if (fin) *gc = 0;
+                    }
+                    fin = __shfl_sync(0x0000ffffu, fin, 0);
+                    if (fin) {
+                        __threadfence();
+                        const float gv = __ldcg(p.partial + (te * 2) * p.b.ff + row);
+                        const float uv = __ldcg(p.partial + (te * 2 + 1) * p.b.ff + row);
+                        p.b.h[te * p.b.ff + row] = gv / (1.f + expf(-gv)) * uv;
+                    }
                 } else {
                     // DOWN: weighted partial; the last of the n_used slots of this
                     // row tile combines them in slot order
@@ -510,8 +627,9 @@ int g_num_sms = 0;
 bool plan_groups(int k, int& wpt, int& gpw) {
     if (k % 128 || k > 2048) return false;
     const int G = k / 128;
+    // even groups per warp: the decode walks whole super-blocks (group pairs)
     for (int w : {4, 3}) {   // P = kConsumers / w <= kMaxP
-        if (kConsumers % w == 0 && kConsumers / w <= kMaxP && G % w == 0 && G / w <= 8) {
+        if (kConsumers % w == 0 && kConsumers / w <= kMaxP && G % w == 0 && G / w <= 8 && (G / w) % 2 == 0) {
             wpt = w;
             gpw = G / w;
             return true;
@@ -531,6 +649,8 @@ int launch(Params& p, cudaStream_t st) {
         g_attr_set = true;
     }
     p.P = kConsumers / p.wpt;
+    p.stage_bytes = (16 * p.rb + 127) & ~127;
+    p.n_stages = std::min(kMaxStages, (kRingBytes / p.stage_bytes) / kIssuers * kIssuers);
     const int grid = std::max(1, std::min(p.n_items, g_num_sms));
     const int tslot = sb_timing_begin(p.mode == MODE_MMID ? "mmid_iq3s" : p.mode == MODE_GATE_UP ? "gate_up_iq3s"
                                                                                                   : "down_iq3s",
@@ -552,27 +672,57 @@ int launch(Params& p, cudaStream_t st) {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
-// scratch of the down kernel: partial sums and self-resetting counters
-float* g_partial = nullptr;
-int* g_counters = nullptr;
-size_t g_partial_cap = 0, g_counter_cap = 0;
+// Scratch of the fused block: the partial sums that CTAs hand to the last
+// finisher of a row tile (gate/up halves; the n_used weighted down partials),
+// and the arrival counters, which the last finisher resets to zero. It grows
+// on demand (cudaMalloc outside any graph capture: the first call of a shape
+// must come before capturing it) and is shared by every call, so calls of the
+// fused block must not overlap on the GPU.
+struct BlockScratch {
+    float* gu_partial = nullptr;   // [T][n_used][2][ff]
+    float* dn_partial = nullptr;   // [T][n_used][d_model]
+    int* gu_counters = nullptr;    // [T][n_used][ff / 16]
+    int* dn_counters = nullptr;    // [T][d_model / 16]
+    void* mem = nullptr;
+    size_t cap = 0;
+    size_t counter_off = 0, counter_bytes = 0;
+    bool stale = false;            // a kernel gave up mid-call: counters may be left non-zero
+};
+BlockScratch g_bs;
 
-bool down_scratch(size_t n_partial, size_t n_counters) {
-    if (n_partial > g_partial_cap) {
-        if (g_partial) cudaFree(g_partial);
-        g_partial = nullptr;
-        g_partial_cap = 0;
-        if (!sb_cuda_ok(cudaMalloc(&g_partial, n_partial * sizeof(float)), "down scratch")) return false;
-        g_partial_cap = n_partial;
+bool block_scratch(int T, int n_used, int d_model, int ff, cudaStream_t st) {
+    const size_t gup = (size_t)T * n_used * 2 * ff, dnp = (size_t)T * n_used * d_model;
+    const size_t guc = (size_t)T * n_used * (ff / 16), dnc = (size_t)T * (d_model / 16);
+    auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t need = up256(gup * 4) + up256(dnp * 4) + up256(guc * 4) + up256(dnc * 4);
+    if (need > g_bs.cap) {
+        if (g_bs.mem) {
+            cudaDeviceSynchronize();   // no kernel of an earlier call may still use it
+            cudaFree(g_bs.mem);
+        }
+        g_bs = BlockScratch{};
+        if (!sb_cuda_ok(cudaMalloc(&g_bs.mem, need), "block scratch")) return false;
+        if (!sb_cuda_ok(cudaMemset(g_bs.mem, 0, need), "block scratch reset")) return false;
+        g_bs.cap = need;
+        g_bs.stale = false;
     }
-    if (n_counters > g_counter_cap) {
-        if (g_counters) cudaFree(g_counters);
-        g_counters = nullptr;
-        g_counter_cap = 0;
-        if (!sb_cuda_ok(cudaMalloc(&g_counters, n_counters * sizeof(int)), "down counters")) return false;
-        if (!sb_cuda_ok(cudaMemset(g_counters, 0, n_counters * sizeof(int)), "down counters reset")) return false;
-        g_counter_cap = n_counters;
+    g_bs.counter_off = up256(gup * 4) + up256(dnp * 4);
+    g_bs.counter_bytes = g_bs.cap - g_bs.counter_off;
+    if (g_bs.stale) {
+        // stream-ordered: runs after every earlier kernel on this stream
+        if (!sb_cuda_ok(cudaMemsetAsync((uint8_t*)g_bs.mem + g_bs.counter_off, 0, g_bs.counter_bytes, st),
+                        "block scratch reset"))
+            return false;
+        g_bs.stale = false;
     }
+    uint8_t* b = (uint8_t*)g_bs.mem;
+    g_bs.gu_partial = (float*)b;
+    b += up256(gup * 4);
+    g_bs.dn_partial = (float*)b;
+    b += up256(dnp * 4);
+    g_bs.gu_counters = (int*)b;
+    b += up256(guc * 4);
+    g_bs.dn_counters = (int*)b;
     return true;
 }
 
@@ -587,12 +737,14 @@ bool fast_path_enabled() {
 
 }  // namespace
 
+void sb_block_scratch_invalidate() { g_bs.stale = g_bs.mem != nullptr; }
+
 int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
     if (a.qt != SB_IQ3_S || !fast_path_enabled()) return 0;
     int wpt, gpw;
     if (!plan_groups(a.k, wpt, gpw) || a.rows % 16) return 0;
     const size_t rb = sb_row_bytes_of(SB_IQ3_S, a.k);
-    if (a.row_stride != rb || 16 * rb > (size_t)kStageBytes) return 0;
+    if (a.row_stride != rb || 16 * rb > (size_t)kMaxTileBytes) return 0;
     if (!a.ex.ptrs && (!aligned16(a.ex.base) || a.ex.expert_stride % 16)) return 0;
     if (a.x_id_stride % 16 || a.x_token_stride % 16 || !aligned16(a.x)) return 0;
     const long long items = (long long)a.n_ids * a.n_tokens * (a.rows / 16);
@@ -617,24 +769,26 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     if (!plan_groups(a.d_model, wpt_g, gpw_g) || !plan_groups(a.ff, wpt_d, gpw_d)) return 0;
     if (a.ff % 16 || a.d_model % 16) return 0;
     const size_t rbg = sb_row_bytes_of(SB_IQ3_S, a.d_model), rbd = sb_row_bytes_of(SB_IQ3_S, a.ff);
-    if (16 * rbg > (size_t)kStageBytes || 16 * rbd > (size_t)kStageBytes) return 0;
+    if (16 * rbg > (size_t)kMaxTileBytes || 16 * rbd > (size_t)kMaxTileBytes) return 0;
     for (const sb_experts* e : {&a.gate, &a.up, &a.down})
         if (!e->ptrs && (!aligned16(e->base) || e->expert_stride % 16)) return 0;
     if (!aligned16(a.x) || !aligned16(a.h) || (a.d_model * 4) % 16 || (a.ff * 4) % 16) return 0;
-    if (!down_scratch((size_t)a.n_tokens * a.n_used * a.d_model, (size_t)a.n_tokens * (a.d_model / 16))) return -1;
+    if (!block_scratch(a.n_tokens, a.n_used, a.d_model, a.ff, st)) return -1;
 
     Params p{};
     p.b = a;
     p.err = a.err;
-    // gate + up + SwiGLU: items (t, e, row tile), each = gate tile + up tile
+    // gate + up + SwiGLU: items (t, e, row tile, gate | up)
     p.mode = MODE_GATE_UP;
     p.rtiles = a.ff / 16;
-    p.n_items = a.n_tokens * a.n_used * p.rtiles;
-    p.per_key = a.n_used * p.rtiles;   // one x per token
+    p.n_items = a.n_tokens * a.n_used * p.rtiles * 2;
+    p.per_key = a.n_used * p.rtiles * 2;   // one x per token
     p.wpt = wpt_g;
     p.gpw = gpw_g;
     p.k = a.d_model;
     p.rb = (int)rbg;
+    p.partial = g_bs.gu_partial;
+    p.counters = g_bs.gu_counters;
     if (launch(p, st) < 0) return -1;
     // down + weighted combine: items (t, e, row tile)
     p.mode = MODE_DOWN;
@@ -645,7 +799,7 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     p.gpw = gpw_d;
     p.k = a.ff;
     p.rb = (int)rbd;
-    p.partial = g_partial;
-    p.counters = g_counters;
+    p.partial = g_bs.dn_partial;
+    p.counters = g_bs.dn_counters;
     return launch(p, st);
 }

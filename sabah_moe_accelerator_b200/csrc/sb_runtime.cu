@@ -494,6 +494,7 @@ bool device_errors_clear() {
     if (g_rt.err_h && *(volatile int*)g_rt.err_h != SB_DERR_NONE) {
         const int code = *(volatile int*)g_rt.err_h;
         *(volatile int*)g_rt.err_h = SB_DERR_NONE;
+        sb_block_scratch_invalidate();
         sb_set_error("%s (device error %d, reported by the first call after the kernel ran)",
                      code == SB_DERR_BAD_ID ? "a kernel found an expert id outside [0, n_experts)"
                      : code == SB_DERR_MISALIGNED ? "an expert base was not 16-byte aligned"
@@ -957,6 +958,7 @@ SABAH_API int sabah_rt_device_error(void) {
     if (!g_rt.err_h) return 0;
     const int c = *(volatile int*)g_rt.err_h;
     *(volatile int*)g_rt.err_h = SB_DERR_NONE;
+    if (c != SB_DERR_NONE) sb_block_scratch_invalidate();
     return c;
 }
 

@@ -674,55 +674,49 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 // Scratch of the fused block: the partial sums that CTAs hand to the last
 // finisher of a row tile (gate/up halves; the n_used weighted down partials),
-// and the arrival counters, which the last finisher resets to zero. It grows
-// on demand (cudaMalloc outside any graph capture: the first call of a shape
-// must come before capturing it) and is shared by every call, so calls of the
-// fused block must not overlap on the GPU.
+// and the arrival counters, which the last finisher resets to zero. Counters
+// sit in their own region at the front, so every shape uses a prefix of the
+// same zeroed words; partial sums follow it. The buffer grows on demand
+// (cudaMalloc outside any graph capture: the first call of a shape must come
+// before capturing it) and is shared by every call, so calls of the fused
+// block must not overlap on the GPU.
 struct BlockScratch {
     float* gu_partial = nullptr;   // [T][n_used][2][ff]
     float* dn_partial = nullptr;   // [T][n_used][d_model]
     int* gu_counters = nullptr;    // [T][n_used][ff / 16]
     int* dn_counters = nullptr;    // [T][d_model / 16]
     void* mem = nullptr;
-    size_t cap = 0;
-    size_t counter_off = 0, counter_bytes = 0;
+    size_t counter_cap = 0, partial_cap = 0;
     bool stale = false;            // a kernel gave up mid-call: counters may be left non-zero
 };
 BlockScratch g_bs;
 
 bool block_scratch(int T, int n_used, int d_model, int ff, cudaStream_t st) {
-    const size_t gup = (size_t)T * n_used * 2 * ff, dnp = (size_t)T * n_used * d_model;
-    const size_t guc = (size_t)T * n_used * (ff / 16), dnc = (size_t)T * (d_model / 16);
     auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
-    const size_t need = up256(gup * 4) + up256(dnp * 4) + up256(guc * 4) + up256(dnc * 4);
-    if (need > g_bs.cap) {
+    const size_t gup = up256((size_t)T * n_used * 2 * ff * 4), dnp = up256((size_t)T * n_used * d_model * 4);
+    const size_t guc = up256((size_t)T * n_used * (ff / 16) * 4), dnc = up256((size_t)T * (d_model / 16) * 4);
+    if (guc + dnc > g_bs.counter_cap || gup + dnp > g_bs.partial_cap) {
+        const size_t ccap = std::max(guc + dnc, g_bs.counter_cap), pcap = std::max(gup + dnp, g_bs.partial_cap);
         if (g_bs.mem) {
             cudaDeviceSynchronize();   // no kernel of an earlier call may still use it
             cudaFree(g_bs.mem);
         }
         g_bs = BlockScratch{};
-        if (!sb_cuda_ok(cudaMalloc(&g_bs.mem, need), "block scratch")) return false;
-        if (!sb_cuda_ok(cudaMemset(g_bs.mem, 0, need), "block scratch reset")) return false;
-        g_bs.cap = need;
-        g_bs.stale = false;
+        if (!sb_cuda_ok(cudaMalloc(&g_bs.mem, ccap + pcap), "block scratch")) return false;
+        if (!sb_cuda_ok(cudaMemset(g_bs.mem, 0, ccap), "block scratch reset")) return false;
+        g_bs.counter_cap = ccap;
+        g_bs.partial_cap = pcap;
     }
-    g_bs.counter_off = up256(gup * 4) + up256(dnp * 4);
-    g_bs.counter_bytes = g_bs.cap - g_bs.counter_off;
     if (g_bs.stale) {
         // stream-ordered: runs after every earlier kernel on this stream
-        if (!sb_cuda_ok(cudaMemsetAsync((uint8_t*)g_bs.mem + g_bs.counter_off, 0, g_bs.counter_bytes, st),
-                        "block scratch reset"))
-            return false;
+        if (!sb_cuda_ok(cudaMemsetAsync(g_bs.mem, 0, g_bs.counter_cap, st), "block scratch reset")) return false;
         g_bs.stale = false;
     }
     uint8_t* b = (uint8_t*)g_bs.mem;
-    g_bs.gu_partial = (float*)b;
-    b += up256(gup * 4);
-    g_bs.dn_partial = (float*)b;
-    b += up256(dnp * 4);
     g_bs.gu_counters = (int*)b;
-    b += up256(guc * 4);
-    g_bs.dn_counters = (int*)b;
+    g_bs.dn_counters = (int*)(b + guc);
+    g_bs.gu_partial = (float*)(b + g_bs.counter_cap);
+    g_bs.dn_partial = (float*)(b + g_bs.counter_cap + gup);
     return true;
 }
 

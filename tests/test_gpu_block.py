@@ -84,3 +84,28 @@ def test_block_ids_config_shape(gpu_rt, orc, qg, qd, T):
                                  d_model, ff, qg, qg, qd)
         r = orc.rel_l2(got[t], want)
         assert r <= TOL and r <= TIGHT, (t, r)
+
+
+def test_block_ids_shape_changes(gpu_rt, orc):
+    """Scratch reuse across shapes: T = 4, then a smaller T = 1, then T = 4 again,
+    each against fp64 (the block's scratch is sized by the largest call so far)."""
+    from sabah_moe_accelerator_b200 import ops
+    d_model, ff, E, K, qt = 2048, 768, 32, 10, 21
+    gate = ops.synth_rows(E * ff, d_model, qt, seed=41, sigma=0.02)
+    up = ops.synth_rows(E * ff, d_model, qt, seed=42, sigma=0.02)
+    down = ops.synth_rows(E * d_model, ff, qt, seed=43, sigma=0.02)
+    g, u, d = gate.cpu().numpy(), up.cpu().numpy(), down.cpu().numpy()
+    for case, T in enumerate((4, 1, 4)):
+        rng = np.random.default_rng(300 + case)
+        ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+        w = rng.random((T, K)).astype(np.float32)
+        w /= w.sum(1, keepdims=True)
+        x = rng.standard_normal((T, d_model)).astype(np.float32)
+        out = ops.moe_block_ids(gate, up, down, torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(),
+                                torch.from_numpy(x).cuda(), d_model, ff, E, qt, qt, qt)
+        got = out.cpu().numpy()
+        for t in range(T):
+            want = orc.moe_block_f64(g.reshape(E, -1), u.reshape(E, -1), d.reshape(E, -1), ids[t], w[t], x[t],
+                                     d_model, ff, qt, qt, qt)
+            r = orc.rel_l2(got[t], want)
+            assert r <= TOL and r <= TIGHT, (case, T, t, r)

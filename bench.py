@@ -155,7 +155,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 (gate_p, up_p, down_p)[role].append(view.data_ptr())
     stream.synchronize()
 
-    ids_np, w_np = routing(ROUTING_SETS)
+    ids_np, w_np = routing(ROUTING_SETS, LAYERS)
     ids_d = torch.from_numpy(ids_np).to(dev)
     w_d = torch.from_numpy(w_np).to(dev)
     x0_d = torch.from_numpy(x0()).to(dev)
@@ -404,13 +404,20 @@ def run_reference(args, rank: int, world: int, local_rank: int):
 
 
 def main():
+    global LAYERS, BYTES_PER_TOKEN, WORKLOAD
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="blocks per token; fewer than 48 only for small profiling cases (not the benchmark)")
     args = ap.parse_args()
+    if args.layers != LAYERS:
+        LAYERS = args.layers
+        BYTES_PER_TOKEN = LAYERS * TOP_K * (2 * GU_EXPERT + D_EXPERT)
+        WORKLOAD = "profiling case (not the benchmark): %d blocks of the cfg2 shape" % LAYERS
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

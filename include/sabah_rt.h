@@ -80,6 +80,26 @@ int sabah_moe_block_ids(const void *gate_bank, const void *up_bank, const void *
                         int n_used, int n_tokens, int qt_gate, int qt_up, int qt_down, int accumulate,
                         void *stream);
 
+/* sabah_moe_block_ids without any allocation. No reference counterpart.
+ * sabah_moe_block_ids grows its cross-CTA scratch with cudaMalloc the first
+ * time it meets a larger shape, which some callers cannot allow: code being
+ * captured into a CUDA graph (an allocation there breaks the capture), a
+ * process whose device memory is carved up before serving starts, or a caller
+ * holding a lock that an implicit device synchronization could deadlock on.
+ * IQ3_S gate, up and down only, d_model and ff in {768, 1024, 1536, 2048}.
+ * Its scratch is a fixed 1 MiB device array: n_tokens * n_used *
+ * (2 * ff + d_model) * 4 bytes must fit in 960 KiB (e.g. 4 tokens x top-10 at
+ * 2048/768), else -1 with the limit in sabah_rt_last_error().
+ * Set-up: the first call on a device (with that device current) looks up the
+ * array's address and queues a clear of its counters on the stream; make that
+ * first call before any stream capture. Calls share the array, so calls that
+ * overlap on the GPU (two streams, two threads) race and give wrong results. */
+int sabah_moe_block_ids_noalloc(const void *gate_bank, const void *up_bank, const void *down_bank,
+                                size_t gu_expert_stride, size_t down_expert_stride, int n_experts,
+                                const int32_t *d_ids, const float *d_w, const float *d_x, float *d_out, float *d_h,
+                                int d_model, int ff, int n_used, int n_tokens, int qt_gate, int qt_up, int qt_down,
+                                int accumulate, void *stream);
+
 /* n_layers routed blocks back to back on one stream with a residual update in
  * place: x <- x + block_L(x) for L = 0..n_layers-1. gate/up/down_banks are HOST
  * arrays of n_layers device pointers; ids/w are [n_layers][n_tokens][n_used] on

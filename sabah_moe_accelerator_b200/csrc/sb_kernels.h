@@ -73,3 +73,6 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);
 // After a device error: the fused block's cross-CTA arrival counters may have
 // been left mid-count by a kernel that gave up; the next call clears them.
 void sb_block_scratch_invalidate();
+// The IQ3_S fused block over a fixed device array instead of allocated scratch
+// (sabah_moe_block_ids_noalloc); -1 with the error set when the call does not fit.
+int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st);

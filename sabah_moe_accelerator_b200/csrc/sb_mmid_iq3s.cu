@@ -720,6 +720,19 @@ bool block_scratch(int T, int n_used, int d_model, int ff, cudaStream_t st) {
     return true;
 }
 
+// Fixed scratch of the allocation-free block (sb_block_iq3s_fixed). Counters
+// occupy the first kFixedCounterBytes whatever the shape; they return to zero
+// after every completed call, so one clearing at set-up (and one after a
+// device error) keeps them valid. The partial sums follow.
+constexpr size_t kFixedScratchBytes = (size_t)1 << 20;    // 1 MiB
+constexpr size_t kFixedCounterBytes = (size_t)64 << 10;   // 16,384 counters
+constexpr int kFixedMaxDevices = 64;
+struct FixedScratch {
+    uint8_t* ptr = nullptr;   // device address of sb_fixed_scratch on this device
+    bool clear = true;        // counters must be zeroed before the next call
+};
+FixedScratch g_fixed[kFixedMaxDevices];
+
 bool fast_path_enabled() {
     static int on = -1;
     if (on < 0) {
@@ -731,7 +744,12 @@ bool fast_path_enabled() {
 
 }  // namespace
 
-void sb_block_scratch_invalidate() { g_bs.stale = g_bs.mem != nullptr; }
+static __device__ __align__(256) uint8_t sb_fixed_scratch[kFixedScratchBytes];
+
+void sb_block_scratch_invalidate() {
+    g_bs.stale = g_bs.mem != nullptr;
+    for (FixedScratch& f : g_fixed) f.clear = true;
+}
 
 int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
     if (a.qt != SB_IQ3_S || !fast_path_enabled()) return 0;
@@ -796,4 +814,81 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     p.partial = g_bs.dn_partial;
     p.counters = g_bs.dn_counters;
     return launch(p, st);
+}
+
+int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st) {
+    if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S) {
+        sb_set_error("the allocation-free block takes IQ3_S gate, up and down only (got %d/%d/%d)", a.qt_gate,
+                     a.qt_up, a.qt_down);
+        return -1;
+    }
+    int wpt_g, gpw_g, wpt_d, gpw_d;
+    if (!plan_groups(a.d_model, wpt_g, gpw_g) || !plan_groups(a.ff, wpt_d, gpw_d) || a.ff % 16 || a.d_model % 16) {
+        sb_set_error("the allocation-free block needs d_model and ff each in {768, 1024, 1536, 2048} (got %d, %d)",
+                     a.d_model, a.ff);
+        return -1;
+    }
+    for (const sb_experts* e : {&a.gate, &a.up, &a.down})
+        if (!aligned16(e->base) || e->expert_stride % 16) {
+            sb_set_error("the allocation-free block needs 16-byte aligned banks and expert strides");
+            return -1;
+        }
+    if (!aligned16(a.x) || !aligned16(a.h)) {
+        sb_set_error("the allocation-free block needs 16-byte aligned x and h");
+        return -1;
+    }
+    auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t slots = (size_t)a.n_tokens * a.n_used;
+    const size_t guc = up256(slots * (a.ff / 16) * 4), dnc = up256((size_t)a.n_tokens * (a.d_model / 16) * 4);
+    const size_t gup = up256(slots * 2 * a.ff * 4), dnp = up256(slots * a.d_model * 4);
+    if (guc + dnc > kFixedCounterBytes || gup + dnp > kFixedScratchBytes - kFixedCounterBytes) {
+        sb_set_error("the allocation-free block needs %zu bytes of partial sums and %zu of counters for %d tokens x %d "
+                     "slots; its fixed scratch holds %zu and %zu",
+                     gup + dnp, guc + dnc, a.n_tokens, a.n_used, kFixedScratchBytes - kFixedCounterBytes,
+                     kFixedCounterBytes);
+        return -1;
+    }
+    int dev = 0;
+    if (!sb_cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return -1;
+    if (dev < 0 || dev >= kFixedMaxDevices) {
+        sb_set_error("the allocation-free block supports devices 0..%d", kFixedMaxDevices - 1);
+        return -1;
+    }
+    FixedScratch& fs = g_fixed[dev];
+    if (!fs.ptr) {
+        void* ptr = nullptr;
+        if (!sb_cuda_ok(cudaGetSymbolAddress(&ptr, sb_fixed_scratch), "fixed scratch address")) return -1;
+        fs.ptr = (uint8_t*)ptr;
+        fs.clear = true;
+    }
+    if (fs.clear) {
+        if (!sb_cuda_ok(cudaMemsetAsync(fs.ptr, 0, kFixedCounterBytes, st), "fixed scratch clear")) return -1;
+        fs.clear = false;
+    }
+
+    Params p{};
+    p.b = a;
+    p.err = a.err;
+    p.mode = MODE_GATE_UP;
+    p.rtiles = a.ff / 16;
+    p.n_items = a.n_tokens * a.n_used * p.rtiles * 2;
+    p.per_key = a.n_used * p.rtiles * 2;
+    p.wpt = wpt_g;
+    p.gpw = gpw_g;
+    p.k = a.d_model;
+    p.rb = (int)sb_row_bytes_of(SB_IQ3_S, a.d_model);
+    p.partial = (float*)(fs.ptr + kFixedCounterBytes);
+    p.counters = (int*)fs.ptr;
+    if (launch(p, st) < 0) return -1;
+    p.mode = MODE_DOWN;
+    p.rtiles = a.d_model / 16;
+    p.n_items = a.n_tokens * a.n_used * p.rtiles;
+    p.per_key = p.rtiles;
+    p.wpt = wpt_d;
+    p.gpw = gpw_d;
+    p.k = a.ff;
+    p.rb = (int)sb_row_bytes_of(SB_IQ3_S, a.ff);
+    p.partial = (float*)(fs.ptr + kFixedCounterBytes + gup);
+    p.counters = (int*)(fs.ptr + guc);
+    return launch(p, st) < 0 ? -1 : 0;
 }

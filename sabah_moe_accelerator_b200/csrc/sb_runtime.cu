@@ -952,6 +952,55 @@ SABAH_API int sabah_moe_block_ids(const void* gate_bank, const void* up_bank, co
     return sb_launch_block(a, stream ? (cudaStream_t)stream : g_rt.compute);
 }
 
+// sabah_moe_block_ids over the fixed scratch of the IQ3_S kernels: no device or
+// host memory is allocated, at the price of a size limit and of calls that
+// must not overlap on the GPU (they share that scratch).
+SABAH_API int sabah_moe_block_ids_noalloc(const void* gate_bank, const void* up_bank, const void* down_bank,
+                                          size_t gu_expert_stride, size_t down_expert_stride, int n_experts,
+                                          const int32_t* d_ids, const float* d_w, const float* d_x, float* d_out,
+                                          float* d_h, int d_model, int ff, int n_used, int n_tokens, int qt_gate,
+                                          int qt_up, int qt_down, int accumulate, void* stream) {
+    if (!ensure_init()) return -1;
+    if (!device_errors_clear()) return -1;
+    if (!gate_bank || !up_bank || !down_bank || !d_ids || !d_w || !d_x || !d_out || !d_h) {
+        sb_set_error("invalid moe_block_ids_noalloc arguments");
+        return -1;
+    }
+    if ((d_model % 32) || (ff % 32) || n_used <= 0 || n_tokens < 0 || n_experts <= 0) {
+        sb_set_error("invalid moe_block_ids_noalloc geometry");
+        return -1;
+    }
+    if (n_tokens == 0) return 0;
+    sb_block_args a{};
+    auto bank = [&](const void* b, size_t stride) {
+        sb_experts e{};
+        e.base = (const uint8_t*)b;
+        e.expert_stride = stride;
+        e.ids = d_ids;
+        e.ids_id_stride = 4;
+        e.ids_token_stride = (size_t)4 * n_used;
+        e.n_experts = n_experts;
+        return e;
+    };
+    a.gate = bank(gate_bank, gu_expert_stride);
+    a.up = bank(up_bank, gu_expert_stride);
+    a.down = bank(down_bank, down_expert_stride);
+    a.x = d_x;
+    a.h = d_h;
+    a.out = d_out;
+    a.w = d_w;
+    a.d_model = d_model;
+    a.ff = ff;
+    a.n_used = n_used;
+    a.n_tokens = n_tokens;
+    a.qt_gate = qt_gate;
+    a.qt_up = qt_up;
+    a.qt_down = qt_down;
+    a.accumulate = accumulate;
+    a.err = g_rt.err_d;
+    return sb_block_iq3s_fixed(a, stream ? (cudaStream_t)stream : g_rt.compute);
+}
+
 // Reads and clears the device error word (1 = an out-of-range expert id met
 // by a kernel reading a device-resident bank). Returns the code, 0 if none.
 SABAH_API int sabah_rt_device_error(void) {

@@ -226,19 +226,22 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     L.sabah_rt_kernel_timing(0)
     ktimes = json.loads(buf.value.decode())
     launches_per_step = sum(v[0] for v in ktimes.values()) / timing_steps
-    # algorithmic bytes per launch of each kernel family
-    kbytes = {
-        "gate_up": TOP_K * 2 * FF * GU_ROW + D_MODEL * 4 + TOP_K * FF * 4,
-        "down": TOP_K * D_MODEL * D_ROW + TOP_K * FF * 4 + 2 * D_MODEL * 4,
-    }
+    # algorithmic bytes per launch of each kernel family: routed expert bytes
+    # once, activations read and written once (x fp32, h fp32)
+    gu_bytes = TOP_K * 2 * FF * GU_ROW + D_MODEL * 4 + TOP_K * FF * 4
+    dn_bytes = TOP_K * D_MODEL * D_ROW + TOP_K * FF * 4 + 2 * D_MODEL * 4
+    kbytes = {"gate_up": gu_bytes, "down": dn_bytes, "decode": LAYERS * (gu_bytes + dn_bytes)}
+    # DRAM bytes per launch from one ncu capture of k_decode_iq3s on the 2-block
+    # case (40.62 MB read + 0.27 MB written), scaled to the blocks decoded
+    traffic = {"decode": int(round((40.62e6 + 0.27e6) / 2 * LAYERS))}
     dom_name, dom = max(ktimes.items(), key=lambda kv: kv[1][1])
-    family = "gate_up" if "gate_up" in dom_name else "down"
+    family = "decode" if "decode" in dom_name else "gate_up" if "gate_up" in dom_name else "down"
     avg_ms = dom[1] / dom[0]
     peaks, peak_kind = measured_peaks()
     achieved = kbytes[family] / (avg_ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "traffic": None, "peak_kind": peak_kind, "bytes_per_launch": kbytes[family],
+                "traffic": traffic.get(family), "peak_kind": peak_kind, "bytes_per_launch": kbytes[family],
                 "avg_launch_us": round(avg_ms * 1e3, 2),
                 "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)} for k, v in ktimes.items()}}
 

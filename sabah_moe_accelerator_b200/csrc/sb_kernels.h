@@ -73,6 +73,28 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);
 // After a device error: the fused block's cross-CTA arrival counters may have
 // been left mid-count by a kernel that gave up; the next call clears them.
 void sb_block_scratch_invalidate();
+// n_layers fused blocks of a decode step in one launch (sabah_moe_decode):
+// x <- x + block_L(x) for L = 0..n_layers-1. Bank pointer arrays are host
+// arrays of device pointers; ids / w are [n_layers][n_tokens][n_used].
+struct sb_decode_args {
+    int n_layers;
+    const void* const* gate_banks;
+    const void* const* up_banks;
+    const void* const* down_banks;
+    size_t gu_expert_stride, down_expert_stride;
+    int n_experts;
+    const int32_t* ids;
+    const float* w;
+    float* x;
+    float* h;
+    int d_model, ff, n_used, n_tokens;
+    int qt_gate, qt_up, qt_down;
+    int* err;
+};
+// persistent IQ3_S decode (sb_decode_iq3s.cu): 1 taken, 0 not covered, -1 error
+int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st);
+void sb_decode_scratch_invalidate();
+
 // The IQ3_S fused block over a fixed device array instead of allocated scratch
 // (sabah_moe_block_ids_noalloc); -1 with the error set when the call does not fit.
 int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st);

@@ -495,6 +495,7 @@ bool device_errors_clear() {
         const int code = *(volatile int*)g_rt.err_h;
         *(volatile int*)g_rt.err_h = SB_DERR_NONE;
         sb_block_scratch_invalidate();
+        sb_decode_scratch_invalidate();
         sb_set_error("%s (device error %d, reported by the first call after the kernel ran)",
                      code == SB_DERR_BAD_ID ? "a kernel found an expert id outside [0, n_experts)"
                      : code == SB_DERR_MISALIGNED ? "an expert base was not 16-byte aligned"
@@ -1007,7 +1008,10 @@ SABAH_API int sabah_rt_device_error(void) {
     if (!g_rt.err_h) return 0;
     const int c = *(volatile int*)g_rt.err_h;
     *(volatile int*)g_rt.err_h = SB_DERR_NONE;
-    if (c != SB_DERR_NONE) sb_block_scratch_invalidate();
+    if (c != SB_DERR_NONE) {
+        sb_block_scratch_invalidate();
+        sb_decode_scratch_invalidate();
+    }
     return c;
 }
 
@@ -1397,6 +1401,33 @@ SABAH_API int sabah_moe_decode(int n_layers, const void* const* gate_banks, cons
     if (!gate_banks || !up_banks || !down_banks || n_layers < 0) {
         sb_set_error("invalid moe_decode arguments");
         return -1;
+    }
+    if (!ensure_init()) return -1;
+    if (!device_errors_clear()) return -1;
+    if (n_layers > 0 && n_tokens > 0 && d_ids && d_w && d_x && d_h && n_used > 0 && n_experts > 0) {
+        // every layer in one persistent launch when the shapes allow it
+        sb_decode_args a{};
+        a.n_layers = n_layers;
+        a.gate_banks = gate_banks;
+        a.up_banks = up_banks;
+        a.down_banks = down_banks;
+        a.gu_expert_stride = gu_expert_stride;
+        a.down_expert_stride = down_expert_stride;
+        a.n_experts = n_experts;
+        a.ids = d_ids;
+        a.w = d_w;
+        a.x = d_x;
+        a.h = d_h;
+        a.d_model = d_model;
+        a.ff = ff;
+        a.n_used = n_used;
+        a.n_tokens = n_tokens;
+        a.qt_gate = qt_gate;
+        a.qt_up = qt_up;
+        a.qt_down = qt_down;
+        a.err = g_rt.err_d;
+        const int taken = sb_try_decode_iq3s(a, stream ? (cudaStream_t)stream : g_rt.compute);
+        if (taken != 0) return taken > 0 ? 0 : -1;
     }
     const size_t per_layer = (size_t)n_tokens * n_used;
     for (int L = 0; L < n_layers; ++L) {

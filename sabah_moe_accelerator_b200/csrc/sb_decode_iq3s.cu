@@ -35,6 +35,11 @@ namespace {
 using namespace sb_iq3s;
 
 constexpr int kNC = 16;                      // consumer warps
+#ifndef SB_DECODE_LOG_R
+#define SB_DECODE_LOG_R 5
+#endif
+constexpr int kLogR = SB_DECODE_LOG_R;       // grid-table replicas: 32, conflict-free lookups
+constexpr int kR = 1 << kLogR;
 constexpr int kThreads = (kNC + 1) * 32;     // + one producer warp
 constexpr int kStageBytes = 16 * 880;        // a 16-row tile at k <= 2048, or two at k <= 1024
 constexpr int kStages = 8;                   // = kIssuers: producer lane l owns stage l
@@ -58,7 +63,7 @@ struct Desc {
 
 struct Smem {
     static constexpr int table = 0;
-    static constexpr int stages = table + kTableBytes;
+    static constexpr int stages = table + table_bytes<kR>();
     static constexpr int sets = stages + kStages * kStageBytes;
     static constexpr int red = sets + kSetArea;                        // [kStages][kMaxWpt][32] floats
     static constexpr int ubuf = red + kStages * kMaxWpt * 32 * 4;      // [kUnits][kMaxUsed][16] floats
@@ -237,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
 
     // ---------------------------------------------------------- consumers
     uint32_t* table = (uint32_t*)(smem + Smem::table);
-    fill_table<kNC * 32>(table);
+    fill_table<kNC * 32, kR>(table);
     const int g = lane >> 2, c = lane & 3;
     const uint32_t boff = lane_boff(lane);
     const uint32_t stages32 = smem_u32(smem + Smem::stages), sets32 = smem_u32(smem + Smem::sets);
@@ -276,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
         const Geo& G = down ? p.dn : p.gu;
         int i0, i1;
         phase_range(p, down, i0, i1);
-        const Lane L = lane_init(table, G.rb, lane);
+        const Lane L = lane_init<kR>(table, G.rb, lane);
         const int P = kNC / G.wpt;
         const int pos = warp / G.wpt, wsub = warp % G.wpt;
 
@@ -326,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                         const int tl = j / G.ppr, q = 2 * (j - tl * G.ppr);
                         if (tl >= d.n) break;
                         float r[2] = {0.f, 0.f};
-                        do_pair(tile0 + (uint32_t)(tl * 16 * G.rb), q, sets32 + (d.slot + tl) * sst + boff, L, r);
+                        do_pair<kLogR>(tile0 + (uint32_t)(tl * 16 * G.rb), q, sets32 + (d.slot + tl) * sst + boff, L, r);
                         acc[0][0] += tl ? 0.f : r[0];
                         acc[0][1] += tl ? 0.f : r[1];
                         acc[1][0] += tl ? r[0] : 0.f;

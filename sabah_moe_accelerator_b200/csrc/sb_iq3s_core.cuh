@@ -13,8 +13,13 @@
 
 namespace sb_iq3s {
 
+// Grid-table replicas: lane l reads replica l % R, so a warp's 32 lookups meet
+// at most 32 / R entries per bank word column (R = 16: 32 KB; R = 32: 64 KB,
+// conflict-free).
 constexpr int kReplicas = 16;
 constexpr int kTableBytes = 512 * kReplicas * 4; // 32 KB
+template <int R>
+constexpr int table_bytes() { return 512 * R * 4; }
 // A producer lane issues its bulk copies one after another (~0.34 us apiece),
 // so kIssuers lanes share the issuing; each owns every kIssuers-th stage.
 constexpr int kIssuers = 8;
@@ -238,7 +243,7 @@ __device__ inline void load_fields(uint32_t r8, uint32_t r4, uint32_t r1, uint32
 
 // Step S (grid entry S of every sub-block) of both groups of a pair: decode
 // rows g and g + 8 of entry S into A fragments and issue the two MMAs.
-template <int S>
+template <int S, int LOG_R>
 __device__ inline void step(uint32_t setq, uint32_t table, const uint32_t (&qsw)[2][2][4], const uint32_t (&QH)[2][2][2],
                             const uint32_t (&sgw)[2][2][4], float (&dd)[2][4]) {
     // PRMT selector: byte 0 = qs byte (S & 1) of the u16 word, byte 1 = QH byte (S & 3), bytes 2, 3 = 0
@@ -253,7 +258,7 @@ __device__ inline void step(uint32_t setq, uint32_t table, const uint32_t (&qsw)
         for (int h = 0; h < 2; ++h) {
             const uint32_t idx = prmt(qsw[n][h][S >> 1], QH[n][h][S >> 2], sel);
             uint32_t grid;
-            asm("ld.shared.u32 %0, [%1];" : "=r"(grid) : "r"((idx << 6) + table));
+            asm("ld.shared.u32 %0, [%1];" : "=r"(grid) : "r"((idx << (LOG_R + 2)) + table));
             const uint32_t Z = ((sgw[n][h][S >> 1] & mask) * kspread) & 0x80808080u;
             a[h][0] = prmt(grid, Z, 0x5140);   // (e0, e1) as signed fp16 subnormals
             a[h][1] = prmt(grid, Z, 0x7362);   // (e2, e3)
@@ -262,17 +267,18 @@ __device__ inline void step(uint32_t setq, uint32_t table, const uint32_t (&qsw)
     }
 }
 
-template <int... S>
+template <int LOG_R, int... S>
 __device__ inline void all_steps(std::integer_sequence<int, S...>, uint32_t setq, uint32_t table,
                                  const uint32_t (&qsw)[2][2][4], const uint32_t (&QH)[2][2][2],
                                  const uint32_t (&sgw)[2][2][4], float (&dd)[2][4]) {
-    (step<S>(setq, table, qsw, QH, sgw, dd), ...);
+    (step<S, LOG_R>(setq, table, qsw, QH, sgw, dd), ...);
 }
 
 // Decode the group pair (q, q + 1), q even (the two halves of super-block q / 2),
 // of a 16-row tile at shared address tile: 2 interleaved MMA chains; adds the
 // sub-block dots of rows g and g + 8 into acc[0] and acc[1]. setB = x-set base
 // + this lane's B-record offset.
+template <int LOG_R = 4>
 __device__ inline void do_pair(uint32_t tile, int q, uint32_t setB, const Lane& L, float (&acc)[2]) {
     const uint32_t sb = tile + (uint32_t)(q >> 1) * 110u;
     const uint32_t setq = setB + (uint32_t)q * kGroupBytes;
@@ -290,7 +296,7 @@ __device__ inline void do_pair(uint32_t tile, int q, uint32_t setB, const Lane& 
     float dd[2][4];
 #pragma unroll
     for (int n = 0; n < 2; ++n) dd[n][0] = dd[n][1] = dd[n][2] = dd[n][3] = 0.f;
-    all_steps(std::make_integer_sequence<int, 8>{}, setq, L.table, qsw, QH, sgw, dd);
+    all_steps<LOG_R>(std::make_integer_sequence<int, 8>{}, setq, L.table, qsw, QH, sgw, dd);
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
         acc[0] = fmaf(db[n][0], dd[n][0] + dd[n][1], acc[0]);
@@ -300,22 +306,23 @@ __device__ inline void do_pair(uint32_t tile, int q, uint32_t setB, const Lane& 
 
 // Replicated grid table: entry e, replica r at word e * kReplicas + r. Threads
 // 0..NT-1 fill it.
-template <int NT>
+template <int NT, int R = kReplicas>
 __device__ inline void fill_table(uint32_t* table) {
     for (int e = threadIdx.x; e < 512; e += NT) {
         const uint32_t w = sb_iq3s_grid[e];
-        uint4* dst = (uint4*)(table + e * kReplicas);
+        uint4* dst = (uint4*)(table + e * R);
 #pragma unroll
-        for (int r = 0; r < kReplicas / 4; ++r) dst[r] = make_uint4(w, w, w, w);
+        for (int r = 0; r < R / 4; ++r) dst[r] = make_uint4(w, w, w, w);
     }
 }
 
 // This lane's constant addresses for tiles with rows of rb bytes.
+template <int R = kReplicas>
 __device__ inline Lane lane_init(const uint32_t* table, int rb, int lane) {
     const int g = lane >> 2, c = lane & 3;
     const int boff = (g >> 1) == c ? (2 * c + (g & 1)) * 8 : 64;
     Lane L;
-    L.table = smem_u32(table) + (lane & (kReplicas - 1)) * 4;
+    L.table = smem_u32(table) + (lane & (R - 1)) * 4;
     L.invd = (uint32_t)(4 * c - boff);
     L.row0 = (uint32_t)(g * rb);
     L.row8c = L.row0 + 8 * c;

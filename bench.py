@@ -73,6 +73,29 @@ def x0():
     return np.random.default_rng(2).standard_normal((1, D_MODEL)).astype(np.float32)
 
 
+# cfg 5: expert-parallel bank
+EP_TOKENS, EP_SETS = 64, 4
+EP_METRIC = "MoE MUL_MAT_ID tokens/s (IQ3_S expert-parallel decode, 64 sequences, 48 x 512-expert bank sharded)"
+EP_WORKLOAD = ("cfg5: IQ3_S expert-parallel decode, 64 sequences x 48 blocks, 512 experts/block sharded "
+               "contiguously over the GPUs, uniform top-10, H2048 F768")
+
+
+def routing_tokens(n_sets: int, n_tok: int, layers: int):
+    """ids/w [n_sets][layers][n_tok][TOP_K]: per token N(0,1) logits over the
+    experts -> softmax -> top-k -> renormalised (uniform routing)."""
+    ids = np.empty((n_sets, layers, n_tok, TOP_K), np.int32)
+    w = np.empty((n_sets, layers, n_tok, TOP_K), np.float32)
+    for s in range(n_sets):
+        for L in range(layers):
+            logits = np.random.default_rng(41 + L + 1000 * s).standard_normal((n_tok, EXPERTS))
+            top = np.argsort(-logits, axis=1, kind="stable")[:, :TOP_K]
+            p = np.exp(logits - logits.max(1, keepdims=True))
+            pt = np.take_along_axis(p, top, 1)
+            ids[s, L] = top
+            w[s, L] = (pt / pt.sum(1, keepdims=True)).astype(np.float32)
+    return ids, w
+
+
 def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -406,6 +429,159 @@ def run_reference(args, rank: int, world: int, local_rank: int):
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_ep(args, rank: int, world: int, local_rank: int):
+    """cfg 5: the bank sharded expert-parallel over the ranks (ep.py), 64
+    sequences decoded one token each per step; NCCL all-gather / reduce-scatter
+    per block. Total work is fixed as N grows (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from sabah_moe_accelerator_b200 import ep, ops, rt
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ops.init(local_rank)
+    L = rt.lib()
+    stream = torch.cuda.Stream(device=dev)
+    st = ctypes.c_void_p(stream.cuda_stream)
+    e0, e1 = ep.expert_range(rank, EXPERTS, world)
+    n_loc = e1 - e0
+    banks = []
+    with torch.cuda.stream(stream):
+        for Lr in range(LAYERS):
+            parts = []
+            for role, rows, k in ((0, FF, D_MODEL), (1, FF, D_MODEL), (2, D_MODEL, FF)):
+                t = torch.empty(n_loc * rows * iq3s_row_bytes(k), dtype=torch.uint8, device=dev)
+                rt.check(L.sabah_synth_rows_at(ctypes.c_void_p(t.data_ptr()), QT_IQ3_S, e0 * rows, n_loc * rows, k,
+                                               (10 + Lr) * 4 + role, 0.02, st), "synth")
+                parts.append(t)
+            banks.append(tuple(parts))
+    stream.synchronize()
+    ids_np, w_np = routing_tokens(EP_SETS, EP_TOKENS, LAYERS)
+    host_plans = [[ep.plan_layer(ids_np[s, Lr], w_np[s, Lr], rank, world, EXPERTS) for Lr in range(LAYERS)]
+                  for s in range(EP_SETS)]
+    plans = [[ep.plan_to_device(pl) for pl in hp] for hp in host_plans]
+    t0, t1 = ep.token_range(rank, EP_TOKENS, world)
+    x_all0 = np.random.default_rng(40).standard_normal((EP_TOKENS, D_MODEL)).astype(np.float32)
+    x0_own = torch.from_numpy(x_all0[t0:t1]).to(dev)
+    x = torch.empty_like(x0_own)
+    comm = ep.TorchComm() if world > 1 else ep.SingleComm()
+    kops = ep.CudaOps(banks, D_MODEL, FF, n_loc, QT_IQ3_S, stream=stream)
+
+    def step(s):
+        x.copy_(x0_own)
+        ep.decode_step(x, plans[s], kops, comm)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i % EP_SETS)
+    stream.synchronize()
+    clocks = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t_0, t_1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t_0.record(stream)
+        for i in range(args.steps):
+            step(i % EP_SETS)
+        t_1.record(stream)
+    stream.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = t_0.elapsed_time(t_1) / args.steps
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # per-kernel device times over one step (eager, events on the launching stream)
+    L.sabah_rt_kernel_timing(1)
+    with torch.cuda.stream(stream):
+        step(0)
+    stream.synchronize()
+    buf = ctypes.create_string_buffer(8192)
+    L.sabah_rt_kernel_times(buf, 8192)
+    L.sabah_rt_kernel_timing(0)
+    ktimes = json.loads(buf.value.decode())
+    launches_per_step = sum(v[0] for v in ktimes.values())
+    # algorithmic bytes: each distinct local expert of a block read once per step
+    # (the pair kernels read an expert once per routed pair; see traffic)
+    distinct = [[int(np.unique(pl.lid).size) for pl in hp] for hp in host_plans]
+    alg_bytes = [sum(n * (2 * GU_EXPERT + D_EXPERT) for n in ds) for ds in distinct]
+    pair_bytes = [sum(pl.n_pairs * (2 * GU_EXPERT + D_EXPERT) for pl in hp) for hp in host_plans]
+    bytes_step = float(np.mean(alg_bytes))
+    peaks, peak_kind = measured_peaks()
+    per_gpu = bytes_step / (ms_max * 1e-3) / 1e9
+    totals = torch.tensor([bytes_step, float(np.mean(pair_bytes))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(totals)
+    roofline = {"bound": "hbm", "kernel": "whole step (gate_up_iq3s + down_iq3s dominate)",
+                "achieved": round(per_gpu, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(per_gpu / peaks["hbm_gbs"], 4), "traffic": int(np.mean(pair_bytes)),
+                "peak_kind": peak_kind, "bytes_per_step_this_gpu": int(bytes_step),
+                "bytes_per_step_all_gpus": int(totals[0].item()), "pair_bytes_per_step_all_gpus": int(totals[1].item()),
+                "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)} for k, v in ktimes.items()}}
+
+    # e2e: host ids planned per step, x from pinned host memory, result back
+    x_h = torch.from_numpy(x_all0[t0:t1].copy()).pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+    h2d = [0]
+
+    def e2e_step(s):
+        x.copy_(x_h, non_blocking=True)
+        pls = []
+        for Lr in range(LAYERS):
+            pl = ep.plan_layer(ids_np[s, Lr], w_np[s, Lr], rank, world, EXPERTS)
+            h2d[0] += pl.tok.nbytes + pl.lid.nbytes + pl.w.nbytes + pl.offsets.nbytes
+            pls.append(ep.plan_to_device(pl))
+        ep.decode_step(x, pls, kops, comm)
+        out_h.copy_(x, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        e2e_step(0)
+    stream.synchronize()
+    barrier()
+    e_steps = max(3, args.steps)
+    h2d[0] = 0
+    e0_, e1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0_.record(stream)
+        for i in range(e_steps):
+            e2e_step(i % EP_SETS)
+        e1_.record(stream)
+    stream.synchronize()
+    e_ms = e0_.elapsed_time(e1_) / e_steps
+    e_t = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
+    e_ms = float(e_t.item())
+    assert np.isfinite(out_h.numpy()).all(), "non-finite decode output"
+    return {
+        "metric": EP_METRIC, "value": round(EP_TOKENS * 1e3 / ms_max, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (N(0,0.02) weights IQ3_S-encoded on device, N(0,1) router logits, N(0,1) x)",
+        "config": {"workload": EP_WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+                   "top_k": TOP_K, "weights": "IQ3_S", "tokens_per_step": EP_TOKENS,
+                   "experts_per_gpu": n_loc, "routing_sets": EP_SETS,
+                   "l2": "inputs larger than L2: ~%.1f GB of distinct expert bytes per step over all GPUs"
+                         % (totals[0].item() / 1e9),
+                   "parallelism": "ep%d" % world, "exchange": "NCCL all-gather + reduce-scatter per block"},
+        "roofline": roofline,
+        "e2e": {"value": round(EP_TOKENS * 1e3 / e_ms, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x_h.numel() * 4 + h2d[0] / e_steps),
+                "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
+                "path": "ep.decode_step (C ABI kernels + NCCL), host plans per step"},
+        "gpu_launches": int(launches_per_step * args.steps),
+        "clocks": clk,
+    }
+
+
 def main():
     global LAYERS, BYTES_PER_TOKEN, WORKLOAD
     ap = argparse.ArgumentParser()
@@ -414,6 +590,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg5"],
+                    help="cfg2: the headline 1-token decode (replicas for N > 1); cfg5: expert-parallel bank")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="blocks per token; fewer than 48 only for small profiling cases (not the benchmark)")
     args = ap.parse_args()
@@ -434,6 +612,8 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     if args.impl == "reference":
         res = run_reference(args, rank, world, local_rank)
+    elif args.workload == "cfg5":
+        res = run_ep(args, rank, world, local_rank)
     else:
         res = run_ours(args, rank, world, local_rank)
     if rank == 0 and res is not None:

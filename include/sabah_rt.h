@@ -205,6 +205,24 @@ int sabah_rt_read_probe(uint64_t off, size_t bytes, char *buf, size_t n);
  * New in this build (the reference reads real GGUF files only). */
 int sabah_synth_rows(void *d_dst, int qt, long long n_rows, int k, unsigned long long seed, float sigma,
                      void *stream);
+/* Rows [row0, row0 + n_rows) of the same tensor (the same bytes a full
+ * sabah_synth_rows call writes there), for one rank's slice of a sharded bank. */
+int sabah_synth_rows_at(void *d_dst, int qt, long long row0, long long n_rows, int k, unsigned long long seed,
+                        float sigma, void *stream);
+
+/* ---- expert-parallel bank (rows of fp32 activations) -------------------------------- */
+
+/* New in this build, for the expert-sharded bank (the reference has one GPU).
+ * dst[i] = src[rows[i]] for i < n; rows of k floats (k % 4 == 0, 16-byte
+ * aligned); an index outside [0, n_src) gives a zero row. Asynchronous. */
+int sabah_ep_gather_rows(const float *d_src, int n_src, const int32_t *d_rows, int n, int k, float *d_dst,
+                         void *stream);
+/* dst[t] = sum of src rows offsets[t] .. offsets[t + 1] - 1 in increasing order
+ * (deterministic), for t < n_out; offsets are clamped to [0, n_src]. Asynchronous. */
+int sabah_ep_sum_rows(const float *d_src, int n_src, const int32_t *d_offsets, int n_out, int k, float *d_dst,
+                      void *stream);
+/* x += y over n floats (n % 4 == 0, 16-byte aligned). Asynchronous. */
+int sabah_ep_add(float *d_x, const float *d_y, long long n, void *stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,120 @@
+// Row movement for the expert-parallel bank: the (token, slot) pairs whose
+// experts live on this GPU are gathered out of the all-gathered activations,
+// pushed through the fused block as one "token" each, and their weighted
+// outputs are summed back into token rows in a fixed order before the
+// reduce-scatter. All three are plain HBM-bound copies / sums of fp32 rows,
+// vectorised as float4 with one warp per row and a grid of 4 CTAs per SM.
+#include <algorithm>
+
+#include "sb_kernels.h"
+
+#define SABAH_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+constexpr int kThreads = 256;   // 8 rows in flight per CTA
+
+int sm_count() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms < 1) sms = 148;
+    }
+    return sms;
+}
+// warps = rows, 8 per CTA; at most 4 CTAs per SM
+int grid_rows(long long rows) { return (int)std::max(1LL, std::min((rows + 7) / 8, 4LL * sm_count())); }
+int grid_elems(long long n4) { return (int)std::max(1LL, std::min((n4 + kThreads - 1) / kThreads, 4LL * sm_count())); }
+
+// dst[i] = src[rows[i]]; a row index outside [0, n_src) gives a zero row
+__global__ void k_gather_rows(const float4* src, int n_src, const int32_t* rows, int n, int k4, float4* dst) {
+    const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = gridDim.x * (kThreads / 32);
+    for (int i = warp; i < n; i += nw) {
+        const int r = rows[i];
+        float4* d = dst + (size_t)i * k4;
+        if (r < 0 || r >= n_src) {
+            for (int j = lane; j < k4; j += 32) d[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            continue;
+        }
+        const float4* s = src + (size_t)r * k4;
+        for (int j = lane; j < k4; j += 32) d[j] = __ldg(s + j);
+    }
+}
+
+// dst[t] = sum_{i in [off[t], off[t+1])} src[i], in increasing i (offsets
+// clamped to [0, n_src])
+__global__ void k_sum_rows(const float4* src, int n_src, const int32_t* off, int n_out, int k4, float4* dst) {
+    const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nw = gridDim.x * (kThreads / 32);
+    for (int t = warp; t < n_out; t += nw) {
+        const int i0 = max(off[t], 0), i1 = min(off[t + 1], n_src);
+        for (int j = lane; j < k4; j += 32) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = i0; i < i1; ++i) {
+                const float4 v = __ldg(src + (size_t)i * k4 + j);
+                a.x += v.x;
+                a.y += v.y;
+                a.z += v.z;
+                a.w += v.w;
+            }
+            dst[(size_t)t * k4 + j] = a;
+        }
+    }
+}
+
+// x += y
+__global__ void k_add(float4* x, const float4* y, long long n4) {
+    for (long long i = blockIdx.x * (long long)kThreads + threadIdx.x; i < n4; i += (long long)gridDim.x * kThreads) {
+        const float4 a = x[i], b = __ldg(y + i);
+        x[i] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+    }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+SABAH_API int sabah_ep_gather_rows(const float* d_src, int n_src, const int32_t* d_rows, int n, int k,
+                                   float* d_dst, void* stream) {
+    if (n < 0 || n_src < 0 || k <= 0 || k % 4 || (n > 0 && (!d_src || !d_rows || !d_dst)) || !aligned16(d_src) ||
+        !aligned16(d_dst)) {
+        sb_set_error("invalid ep gather arguments (n %d, k %d)", n, k);
+        return -1;
+    }
+    if (n == 0) return 0;
+    const int tslot = sb_timing_begin("ep_gather_rows", (cudaStream_t)stream);
+    k_gather_rows<<<grid_rows(n), kThreads, 0, (cudaStream_t)stream>>>((const float4*)d_src, n_src, d_rows, n,
+                                                                       k / 4, (float4*)d_dst);
+    sb_timing_end(tslot, (cudaStream_t)stream);
+    return sb_cuda_ok(cudaGetLastError(), "ep gather launch") ? 0 : -1;
+}
+
+SABAH_API int sabah_ep_sum_rows(const float* d_src, int n_src, const int32_t* d_offsets, int n_out, int k,
+                                float* d_dst, void* stream) {
+    if (n_out < 0 || n_src < 0 || k <= 0 || k % 4 || (n_out > 0 && (!d_offsets || !d_dst)) ||
+        (n_src > 0 && !d_src) || !aligned16(d_src) || !aligned16(d_dst)) {
+        sb_set_error("invalid ep sum arguments (n_out %d, k %d)", n_out, k);
+        return -1;
+    }
+    if (n_out == 0) return 0;
+    const int tslot = sb_timing_begin("ep_sum_rows", (cudaStream_t)stream);
+    k_sum_rows<<<grid_rows(n_out), kThreads, 0, (cudaStream_t)stream>>>((const float4*)d_src, n_src, d_offsets, n_out,
+                                                                        k / 4, (float4*)d_dst);
+    sb_timing_end(tslot, (cudaStream_t)stream);
+    return sb_cuda_ok(cudaGetLastError(), "ep sum launch") ? 0 : -1;
+}
+
+SABAH_API int sabah_ep_add(float* d_x, const float* d_y, long long n, void* stream) {
+    if (n < 0 || n % 4 || (n > 0 && (!d_x || !d_y)) || !aligned16(d_x) || !aligned16(d_y)) {
+        sb_set_error("invalid ep add arguments (n %lld)", n);
+        return -1;
+    }
+    if (n == 0) return 0;
+    const int tslot = sb_timing_begin("ep_add", (cudaStream_t)stream);
+    k_add<<<grid_elems(n / 4), kThreads, 0, (cudaStream_t)stream>>>((float4*)d_x, (const float4*)d_y, n / 4);
+    sb_timing_end(tslot, (cudaStream_t)stream);
+    return sb_cuda_ok(cudaGetLastError(), "ep add launch") ? 0 : -1;
+}

@@ -62,16 +62,18 @@ __global__ void k_iq3s_nearest(uint16_t* out) {
     out[code] = (uint16_t)best;
 }
 
-// One thread encodes one block. Element n of the tensor is row * k + column.
+// One thread encodes one block. Element n of the tensor is (row0 + row) * k +
+// column, so rows [row0, row0 + n_rows) of a larger tensor can be made alone.
 template <int QT>
-__global__ void k_synth(uint8_t* dst, long long n_rows, int k, uint64_t seed, float sigma, const uint16_t* nearest) {
+__global__ void k_synth(uint8_t* dst, long long row0, long long n_rows, int k, uint64_t seed, float sigma,
+                        const uint16_t* nearest) {
     const int be = sb_block_elems(QT), bb = sb_block_bytes(QT);
     const int bpr = k / be;
     const long long nblk = n_rows * bpr;
     for (long long b = blockIdx.x * (long long)blockDim.x + threadIdx.x; b < nblk; b += (long long)gridDim.x * blockDim.x) {
         const long long row = b / bpr;
         const int col0 = (int)(b % bpr) * be;
-        const uint64_t n0 = (uint64_t)row * (uint64_t)k + (uint64_t)col0;
+        const uint64_t n0 = (uint64_t)(row0 + row) * (uint64_t)k + (uint64_t)col0;
         uint8_t* o = dst + (size_t)b * bb;
         auto v = [&](int i) { return normal_at(seed, n0 + (uint64_t)i, sigma); };
         if constexpr (QT == SB_Q8_0) {
@@ -180,12 +182,12 @@ uint16_t* g_nearest = nullptr;
 
 }  // namespace
 
-// Fill d_dst with n_rows rows of k elements of type qt (dense rows), weights
-// N(0, sigma) from `seed`. Supported: Q8_0, Q4_K, Q6_K, IQ3_S. Asynchronous on
-// `stream` (NULL: the legacy default stream).
-SABAH_API int sabah_synth_rows(void* d_dst, int qt, long long n_rows, int k, unsigned long long seed, float sigma,
-                               void* stream) {
-    if (!d_dst || n_rows < 0 || k <= 0 || !sb_row_bytes_of(qt, k)) {
+// Fill d_dst with rows [row0, row0 + n_rows) of a tensor of rows of k elements
+// of type qt (dense rows), weights N(0, sigma) from `seed`. Supported: Q8_0,
+// Q4_K, Q6_K, IQ3_S. Asynchronous on `stream` (NULL: the legacy default stream).
+SABAH_API int sabah_synth_rows_at(void* d_dst, int qt, long long row0, long long n_rows, int k,
+                                  unsigned long long seed, float sigma, void* stream) {
+    if (!d_dst || n_rows < 0 || row0 < 0 || k <= 0 || !sb_row_bytes_of(qt, k)) {
         sb_set_error("invalid synth geometry (type %d, k %d)", qt, k);
         return -1;
     }
@@ -198,13 +200,18 @@ SABAH_API int sabah_synth_rows(void* d_dst, int qt, long long n_rows, int k, uns
     const int grid = (int)std::min<long long>((nblk + 255) / 256, 148LL * 64);
     uint8_t* d = (uint8_t*)d_dst;
     switch (qt) {
-    case SB_Q8_0: k_synth<SB_Q8_0><<<grid, 256, 0, st>>>(d, n_rows, k, seed, sigma, g_nearest); break;
-    case SB_Q4_K: k_synth<SB_Q4_K><<<grid, 256, 0, st>>>(d, n_rows, k, seed, sigma, g_nearest); break;
-    case SB_Q6_K: k_synth<SB_Q6_K><<<grid, 256, 0, st>>>(d, n_rows, k, seed, sigma, g_nearest); break;
-    case SB_IQ3_S: k_synth<SB_IQ3_S><<<grid, 256, 0, st>>>(d, n_rows, k, seed, sigma, g_nearest); break;
+    case SB_Q8_0: k_synth<SB_Q8_0><<<grid, 256, 0, st>>>(d, row0, n_rows, k, seed, sigma, g_nearest); break;
+    case SB_Q4_K: k_synth<SB_Q4_K><<<grid, 256, 0, st>>>(d, row0, n_rows, k, seed, sigma, g_nearest); break;
+    case SB_Q6_K: k_synth<SB_Q6_K><<<grid, 256, 0, st>>>(d, row0, n_rows, k, seed, sigma, g_nearest); break;
+    case SB_IQ3_S: k_synth<SB_IQ3_S><<<grid, 256, 0, st>>>(d, row0, n_rows, k, seed, sigma, g_nearest); break;
     default:
         sb_set_error("synth: quant type %d has no encoder", qt);
         return -1;
     }
     return sb_cuda_ok(cudaGetLastError(), "synth launch") ? 0 : -1;
+}
+
+SABAH_API int sabah_synth_rows(void* d_dst, int qt, long long n_rows, int k, unsigned long long seed, float sigma,
+                               void* stream) {
+    return sabah_synth_rows_at(d_dst, qt, 0, n_rows, k, seed, sigma, stream);
 }

@@ -107,6 +107,10 @@ SIGNATURES = {
     "sabah_rt_kernel_timing": ([c_i], c_i),
     "sabah_rt_kernel_times": ([ctypes.c_char_p, c_sz], c_i),
     "sabah_synth_rows": ([c_vp, c_i, ctypes.c_longlong, c_i, ctypes.c_ulonglong, c_f, c_vp], c_i),
+    "sabah_synth_rows_at": ([c_vp, c_i, ctypes.c_longlong, ctypes.c_longlong, c_i, ctypes.c_ulonglong, c_f, c_vp], c_i),
+    "sabah_ep_gather_rows": ([c_vp, c_i, c_vp, c_i, c_i, c_vp, c_vp], c_i),
+    "sabah_ep_sum_rows": ([c_vp, c_i, c_vp, c_i, c_i, c_vp, c_vp], c_i),
+    "sabah_ep_add": ([c_vp, c_vp, ctypes.c_longlong, c_vp], c_i),
 }
 
 

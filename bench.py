@@ -582,6 +582,110 @@ def run_ep(args, rank: int, world: int, local_rank: int):
     }
 
 
+PF_TOKENS, PF_SETS = 512, 4
+PF_METRIC = "MoE MUL_MAT_ID tokens/s (IQ3_S prefill, 512 tokens through one block, gate + up + down)"
+PF_WORKLOAD = ("cfg3: IQ3_S prefill, 512 tokens x 1 block (gate, up, down MUL_MAT_ID), 512 experts, top-10, "
+               "Zipf(1.1) expert popularity, H2048 F768")
+
+
+def zipf_routing(n_sets: int, n_tok: int, seed: int = 20):
+    """ids [n_sets][n_tok][TOP_K]: per token 10 distinct experts drawn with
+    probability proportional to rank^-1.1 under a seeded rank permutation."""
+    ids = np.empty((n_sets, n_tok, TOP_K), np.int32)
+    w = np.empty((n_sets, n_tok, TOP_K), np.float32)
+    p = 1.0 / np.arange(1, EXPERTS + 1) ** 1.1
+    p /= p.sum()
+    for s in range(n_sets):
+        rng = np.random.default_rng(seed + s)
+        perm = rng.permutation(EXPERTS)
+        for t in range(n_tok):
+            ids[s, t] = perm[rng.choice(EXPERTS, TOP_K, replace=False, p=p)]
+        ww = rng.random((n_tok, TOP_K)).astype(np.float32)
+        w[s] = ww / ww.sum(1, keepdims=True)
+    return ids, w
+
+
+def run_prefill(args, rank: int, world: int, local_rank: int):
+    """cfg 3: the three MUL_MAT_ID calls of one block over 512 prefill tokens
+    through the v2 C ABI on a device-resident bank (grouped tcgen05 path)."""
+    import torch
+    from sabah_moe_accelerator_b200 import ops, rt
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ops.init(local_rank)
+    L = rt.lib()
+    stream = torch.cuda.Stream(device=dev)
+    T, K = PF_TOKENS, TOP_K
+    with torch.cuda.stream(stream):
+        gate = ops.synth_rows(EXPERTS * FF, D_MODEL, QT_IQ3_S, seed=101, sigma=0.02, stream=stream)
+        up = ops.synth_rows(EXPERTS * FF, D_MODEL, QT_IQ3_S, seed=102, sigma=0.02, stream=stream)
+        down = ops.synth_rows(EXPERTS * D_MODEL, FF, QT_IQ3_S, seed=103, sigma=0.02, stream=stream)
+    stream.synchronize()
+    ids_np, _ = zipf_routing(PF_SETS, T)
+    ids_d = [torch.from_numpy(ids_np[s]).to(dev) for s in range(PF_SETS)]
+    x = torch.from_numpy(np.random.default_rng(22).standard_normal((T, 1, D_MODEL)).astype(np.float32)).to(dev)
+    g_out = torch.empty((T, K, FF), device=dev)
+    u_out = torch.empty((T, K, FF), device=dev)
+    h = torch.from_numpy(np.random.default_rng(23).standard_normal((T, K, FF)).astype(np.float32) * 0.5).to(dev)
+    d_out = torch.empty((T, K, D_MODEL), device=dev)
+
+    def step(s):
+        ops.mul_mat_id(gate, GU_EXPERT, GU_ROW, x, ids_d[s], FF, D_MODEL, EXPERTS, QT_IQ3_S, out=g_out, stream=stream)
+        ops.mul_mat_id(up, GU_EXPERT, GU_ROW, x, ids_d[s], FF, D_MODEL, EXPERTS, QT_IQ3_S, out=u_out, stream=stream)
+        ops.mul_mat_id(down, D_EXPERT, D_ROW, h, ids_d[s], D_MODEL, FF, EXPERTS, QT_IQ3_S, out=d_out, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i % PF_SETS)
+    stream.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(args.steps):
+            step(i % PF_SETS)
+        t1.record(stream)
+    stream.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    # kernel times of one step
+    L.sabah_rt_kernel_timing(1)
+    with torch.cuda.stream(stream):
+        step(0)
+    stream.synchronize()
+    buf = ctypes.create_string_buffer(8192)
+    L.sabah_rt_kernel_times(buf, 8192)
+    L.sabah_rt_kernel_timing(0)
+    ktimes = json.loads(buf.value.decode())
+    distinct = np.mean([np.unique(ids_np[s]).size for s in range(PF_SETS)])
+    alg_bytes = distinct * (2 * GU_EXPERT + D_EXPERT) + T * D_MODEL * 4 + 2 * T * K * FF * 4 * 2 + T * K * D_MODEL * 4
+    flops = 2.0 * T * K * (2 * FF * D_MODEL + D_MODEL * FF)
+    peaks, peak_kind = measured_peaks()
+    gbs = alg_bytes / (ms * 1e-3) / 1e9
+    tfs = flops / (ms * 1e-3) / 1e12
+    return {
+        "metric": PF_METRIC, "value": round(T * 1e3 / ms, 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp16 hi/lo operands, fp32 accumulate)",
+        "data": "synthetic (N(0,0.02) weights IQ3_S-encoded on device, Zipf(1.1) routing, N(0,1) x)",
+        "config": {"workload": PF_WORKLOAD, "tokens": T, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+                   "top_k": K, "distinct_experts_per_step": float(distinct), "routing_sets": PF_SETS,
+                   "l2": "weights of ~%d distinct experts (%.2f GB) per step, 4 routing sets cycled"
+                         % (distinct, distinct * (2 * GU_EXPERT + D_EXPERT) / 1e9)},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None, "peak_kind": peak_kind,
+                     "tensor": {"achieved_tflops": round(tfs, 1), "peak_tflops": peaks.get("bf16_tflops"),
+                                "frac": round(tfs / peaks.get("bf16_tflops", 1590.0), 4),
+                                "note": "algorithmic FLOPs; the kernel issues 3 fp16 MMAs per product (hi/lo split)"},
+                     "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)}
+                                 for k, v in ktimes.items()}},
+        "gpu_launches": int(sum(v[0] for v in ktimes.values()) * args.steps),
+        "clocks": clk,
+    }
+
+
 def main():
     global LAYERS, BYTES_PER_TOKEN, WORKLOAD
     ap = argparse.ArgumentParser()
@@ -590,8 +694,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg5"],
-                    help="cfg2: the headline 1-token decode (replicas for N > 1); cfg5: expert-parallel bank")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg5"],
+                    help="cfg2: the headline 1-token decode (replicas for N > 1); cfg3: 512-token prefill "
+                         "of one block; cfg5: expert-parallel bank")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="blocks per token; fewer than 48 only for small profiling cases (not the benchmark)")
     args = ap.parse_args()
@@ -614,6 +719,8 @@ def main():
         res = run_reference(args, rank, world, local_rank)
     elif args.workload == "cfg5":
         res = run_ep(args, rank, world, local_rank)
+    elif args.workload == "cfg3":
+        res = run_prefill(args, rank, world, local_rank) if rank == 0 else None
     else:
         res = run_ours(args, rank, world, local_rank)
     if rank == 0 and res is not None:

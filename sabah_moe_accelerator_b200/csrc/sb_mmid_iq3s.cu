@@ -485,6 +485,8 @@ void sb_block_scratch_invalidate() {
 
 int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
     if (a.qt != SB_IQ3_S || !fast_path_enabled()) return 0;
+    const int grouped = sb_try_mmid_iq3s_grouped(a, st);   // prefill-sized calls
+    if (grouped != 0) return grouped;
     int wpt, gpw;
     if (!plan_groups(a.k, wpt, gpw) || a.rows % 16) return 0;
     const size_t rb = sb_row_bytes_of(SB_IQ3_S, a.k);

@@ -76,7 +76,7 @@ struct PairInfo {
     long long x_off;    // byte offset of the pair's x row
     long long dst_off;  // byte offset of the pair's dst row
     int exp;            // x scale: the row is multiplied by 2^exp before the fp16 split
-    int pad;
+    int xrow;           // the x row: t * x_rows + i % x_rows
 };
 
 struct GemmParams {
@@ -479,8 +479,11 @@ struct GroupParams {
     size_t dst_id_stride, dst_token_stride;
     int* counts;      // [n_experts]
     int* cursor;      // [n_experts]
-    Task* tasks;
+    Task* tasks;      // tcgen05 tasks: experts with >= heavy pairs
     int* n_tasks;
+    Task* mtasks;     // register-decode tasks: (expert, 16-row tile) of experts with < heavy pairs
+    int* n_mtasks;
+    int heavy, r_tiles16;
     int* order;       // [pairs] pair index in grouped order
     PairInfo* pairs;  // [pairs] grouped order
     int* err;
@@ -510,34 +513,46 @@ __global__ void k_group_count(const GroupParams g) {
 
 // one CTA of 1024 threads: exclusive scans of the counts and of the tasks per expert
 __global__ void k_group_plan(const GroupParams g) {
-    __shared__ int s_sum[1024], s_tsum[1024];
+    __shared__ int s_sum[1024], s_tsum[1024], s_msum[1024];
     const int E = g.n_experts, per = (E + 1023) / 1024;
     const int e0 = threadIdx.x * per, e1 = min(E, e0 + per);
-    int c = 0, tc = 0;
+    int c = 0, tc = 0, mc = 0;
     for (int e = e0; e < e1; ++e) {
-        c += g.counts[e];
-        tc += (g.counts[e] + kMaxN - 1) / kMaxN * g.m_tiles;
+        const int ce = g.counts[e];
+        c += ce;
+        if (ce >= g.heavy) tc += (ce + kMaxN - 1) / kMaxN * g.m_tiles;
+        else if (ce > 0) mc += g.r_tiles16;
     }
     s_sum[threadIdx.x] = c;
     s_tsum[threadIdx.x] = tc;
+    s_msum[threadIdx.x] = mc;
     __syncthreads();
-    for (int off = 1; off < 1024; off <<= 1) {   // inclusive Hillis-Steele scan
+    for (int off = 1; off < 1024; off <<= 1) {   // inclusive Hillis-Steele scans
         const int a = threadIdx.x >= off ? s_sum[threadIdx.x - off] : 0;
         const int b = threadIdx.x >= off ? s_tsum[threadIdx.x - off] : 0;
+        const int m = threadIdx.x >= off ? s_msum[threadIdx.x - off] : 0;
         __syncthreads();
         s_sum[threadIdx.x] += a;
         s_tsum[threadIdx.x] += b;
+        s_msum[threadIdx.x] += m;
         __syncthreads();
     }
-    int pos = s_sum[threadIdx.x] - c, tpos = s_tsum[threadIdx.x] - tc;
+    int pos = s_sum[threadIdx.x] - c, tpos = s_tsum[threadIdx.x] - tc, mpos = s_msum[threadIdx.x] - mc;
     for (int e = e0; e < e1; ++e) {
         const int ce = g.counts[e];
         g.cursor[e] = pos;
-        for (int n0 = 0; n0 < ce; n0 += kMaxN)
-            for (int mt = 0; mt < g.m_tiles; ++mt) g.tasks[tpos++] = Task{e, mt, pos + n0, min(kMaxN, ce - n0)};
+        if (ce >= g.heavy) {
+            for (int n0 = 0; n0 < ce; n0 += kMaxN)
+                for (int mt = 0; mt < g.m_tiles; ++mt) g.tasks[tpos++] = Task{e, mt, pos + n0, min(kMaxN, ce - n0)};
+        } else if (ce > 0) {
+            for (int rt = 0; rt < g.r_tiles16; ++rt) g.mtasks[mpos++] = Task{e, rt, pos, ce};
+        }
         pos += ce;
     }
-    if (threadIdx.x == 1023) *g.n_tasks = s_tsum[1023];
+    if (threadIdx.x == 1023) {
+        *g.n_tasks = s_tsum[1023];
+        *g.n_mtasks = s_msum[1023];
+    }
 }
 
 __global__ void k_group_scatter(const GroupParams g, uint8_t* dst, int rows) {
@@ -574,9 +589,217 @@ __global__ void k_group_pairs(const GroupParams g) {
                 frexpf(m, &ex);
                 ex = max(-100, min(100, 14 - ex));
             }
-            g.pairs[q] = PairInfo{xo, (long long)(t * g.dst_token_stride + i * g.dst_id_stride), ex, 0};
+            g.pairs[q] = PairInfo{xo, (long long)(t * g.dst_token_stride + i * g.dst_id_stride), ex,
+                                  t * g.x_rows + i % g.x_rows};
         }
     }
+}
+
+// Each x row (t, x_row) scaled by 2^exp (max -> [2^13, 2^14)) and split into
+// fp16 hi / lo (truncated hi, exact; lo rounded), one warp per row.
+__global__ void k_x_split(const uint8_t* x, size_t x_id_stride, size_t x_token_stride, int x_rows, int n_rows, int k,
+                          __half* xh, __half* xl, int* xexp) {
+    const int nw = gridDim.x * (blockDim.x / 32);
+    const int lane = threadIdx.x & 31;
+    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32; row < n_rows; row += nw) {
+        const float* xr = (const float*)(x + (size_t)(row / x_rows) * x_token_stride + (size_t)(row % x_rows) * x_id_stride);
+        float m = 0.f;
+        for (int kk = lane; kk < k; kk += 32) m = fmaxf(m, fabsf(xr[kk]));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        int ex = 0;
+        if (m > 0.f && isfinite(m)) {
+            frexpf(m, &ex);
+            ex = max(-100, min(100, 14 - ex));
+        }
+        const float sc = ldexpf(1.f, ex);
+        if (lane == 0) xexp[row] = ex;
+        for (int kk = 2 * lane; kk < k; kk += 64) {
+            const float a = xr[kk] * sc, b = xr[kk + 1] * sc;
+            const float ah = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+            const float bh = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
+            *(__half2*)(xh + (size_t)row * k + kk) = __floats2half2_rn(ah, bh);
+            *(__half2*)(xl + (size_t)row * k + kk) = __floats2half2_rn(a - ah, b - bh);
+        }
+    }
+}
+
+// ------------------------------------------------------------ register-decode grouped kernel
+// For experts with few pairs. A warp owns a task (expert, 16-row tile, all of
+// the expert's n < heavy pairs): the tile lands in the warp's shared-memory
+// buffer by one bulk copy; per IQ3_S sub-block the warp decodes its A
+// fragments once (mma.sync m16n8k16 layout; the MMA's k slots {2c, 2c+1,
+// 2c+8, 2c+9} are mapped to the 4 weights of grid entry c, so one grid lookup
+// gives a thread its fragment, placed as fp16 subnormals b * 2^-24 with their
+// signs) and multiplies them with each group of 8 pairs' x (fp16 hi and lo
+// parts, split once per x row); the sub-block's scale is applied to the
+// group's fp32 partial sums.
+constexpr int kGW = 12;                      // warps per CTA
+constexpr int kGTile = 16 * 880;             // a 16-row tile at k <= 2048
+constexpr int kGRep = 8;                     // grid-table replicas
+constexpr int kGMaxGroups = 8;               // pairs per task < 64
+
+struct MmaSmem {
+    static constexpr int grid = 0;                          // [512][kGRep] u32
+    static constexpr int tiles = grid + 512 * kGRep * 4;    // [kGW][kGTile]
+    static constexpr int bars = tiles + kGW * kGTile;       // [kGW]
+    static constexpr int total = bars + kGW * 8;
+};
+static_assert(MmaSmem::total <= 227 * 1024, "shared memory budget");
+static_assert(MmaSmem::tiles % 16 == 0 && kGTile % 16 == 0, "bulk-copy alignment");
+
+struct MmaParams {
+    const uint8_t* base;
+    size_t expert_stride;
+    int rb, k;
+    const Task* tasks;
+    const int* n_tasks;
+    const PairInfo* pairs;
+    const __half* xh;
+    const __half* xl;
+    const int* xexp;
+    uint8_t* dst;
+    int* err;
+};
+
+__device__ inline void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(kGW * 32, 1) k_group_mma_iq3s(const MmaParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    uint32_t* gtab = (uint32_t*)(smem + MmaSmem::grid);
+    uint8_t* tile = smem + MmaSmem::tiles + warp * kGTile;
+    const uint32_t bar = smem_u32(smem + MmaSmem::bars + warp * 8);
+    for (int e = threadIdx.x; e < 512; e += kGW * 32) {
+        const uint32_t w = sb_iq3s_grid[e];
+#pragma unroll
+        for (int r = 0; r < kGRep; ++r) gtab[e * kGRep + r] = w;
+    }
+    if (lane == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const int n_tasks = *p.n_tasks;
+    const uint32_t bytes = (uint32_t)(16 * p.rb);
+    const int stride = gridDim.x * kGW;
+    const uint32_t grep = (uint32_t)(lane & (kGRep - 1));
+    uint32_t phase = 0;
+    bool failed = false;
+    for (int ti = blockIdx.x * kGW + warp; ti < n_tasks; ti += stride) {
+        const Task t = p.tasks[ti];
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // earlier reads of the buffer
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                             smem_u32(tile)),
+                         "l"(p.base + (size_t)t.expert * p.expert_stride + (size_t)t.mt * bytes), "r"(bytes), "r"(bar)
+                         : "memory");
+            if (ti + stride < n_tasks) {   // the next task's tile, into L2 meanwhile
+                const Task tn = p.tasks[ti + stride];
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                                 p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * bytes),
+                             "r"(bytes)
+                             : "memory");
+            }
+        }
+        // this lane's pair in each group of 8: n = 8 * gr + g
+        const int ng = (t.n + 7) >> 3;
+        int xr[kGMaxGroups];
+#pragma unroll
+        for (int gr = 0; gr < kGMaxGroups; ++gr) {
+            const int n = 8 * gr + g;
+            xr[gr] = (gr < ng && n < t.n) ? p.pairs[t.n0 + n].xrow : -1;
+        }
+        bool ok = true;
+        {
+            long long it = 0;
+            while (!mbar_try_wait(bar, phase) && ++it < kSpinLimit) {
+            }
+            ok = it < kSpinLimit;
+        }
+        if (!__all_sync(0xffffffffu, ok)) {   // the copy of this phase is still outstanding
+            if (lane == 0 && p.err) atomicExch(p.err, SB_DERR_TIMEOUT);
+            failed = true;
+            break;
+        }
+        phase ^= 1;
+        float acc[kGMaxGroups][4];
+#pragma unroll
+        for (int gr = 0; gr < kGMaxGroups; ++gr) acc[gr][0] = acc[gr][1] = acc[gr][2] = acc[gr][3] = 0.f;
+        for (int sb = 0; sb < p.k / 32; ++sb) {
+            const int j = sb >> 3, ib = sb & 7;
+            uint32_t a[2][2][2];   // [k16 half q][row h][reg]
+            float db[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint8_t* rb = tile + (size_t)(g + 8 * h) * p.rb + j * 110;
+                const float d = __half2float(__ushort_as_half(*(const unsigned short*)rb));
+                const unsigned nib = (rb[106 + (ib >> 1)] >> (4 * (ib & 1))) & 15u;
+                db[h] = d * (float)(1 + 2 * (int)nib) * 16777216.f;   // 2^24 undoes the subnormal encoding
+                const unsigned qh = rb[66 + ib];
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int e = 4 * q + c;
+                    const uint32_t idx = rb[2 + 8 * ib + e] | (((qh >> e) & 1u) << 8);
+                    const uint32_t gw = gtab[idx * kGRep + grep];
+                    const uint32_t sg = (rb[74 + 4 * ib + (e >> 1)] >> (4 * (e & 1))) & 15u;
+                    const uint32_t Z = (sg * 0x10204080u) & 0x80808080u;   // sign bit i -> bit 7 of byte i
+                    a[q][h][0] = prmt(gw, Z, 0x5140);   // (w0, w1) as signed fp16 subnormals
+                    a[q][h][1] = prmt(gw, Z, 0x7362);   // (w2, w3)
+                }
+            }
+#pragma unroll
+            for (int gr = 0; gr < kGMaxGroups; ++gr) {
+                if (gr >= ng) break;
+                uint2 bh[2] = {make_uint2(0, 0), make_uint2(0, 0)}, bl[2] = {make_uint2(0, 0), make_uint2(0, 0)};
+                if (xr[gr] >= 0) {
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const size_t off = (size_t)xr[gr] * p.k + 32 * sb + 16 * q + 4 * c;
+                        bh[q] = __ldg((const uint2*)(p.xh + off));
+                        bl[q] = __ldg((const uint2*)(p.xl + off));
+                    }
+                }
+                float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bh[q].x, bh[q].y);
+                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bl[q].x, bl[q].y);
+                }
+                acc[gr][0] = fmaf(db[0], dd[0], acc[gr][0]);
+                acc[gr][1] = fmaf(db[0], dd[1], acc[gr][1]);
+                acc[gr][2] = fmaf(db[1], dd[2], acc[gr][2]);
+                acc[gr][3] = fmaf(db[1], dd[3], acc[gr][3]);
+            }
+        }
+        // D: (row g, pair 2c), (row g, pair 2c + 1), (row g + 8, pair 2c), (row g + 8, pair 2c + 1)
+#pragma unroll
+        for (int gr = 0; gr < kGMaxGroups; ++gr) {
+            if (gr >= ng) break;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int n = 8 * gr + 2 * c + u;
+                if (n >= t.n) continue;
+                const PairInfo pi = p.pairs[t.n0 + n];
+                float* d = (float*)(p.dst + pi.dst_off) + t.mt * 16;
+                const int ex = p.xexp[pi.xrow];
+                d[g] = ldexpf(acc[gr][u], -ex);
+                d[g + 8] = ldexpf(acc[gr][2 + u], -ex);
+            }
+        }
+        __syncwarp();   // every lane is done with the tile before the next copy overwrites it
+    }
+    // never leave with a copy in flight
+    if (failed && lane == 0)
+        for (long long it = 0; it < kSpinLimit && !mbar_try_wait(bar, phase); ++it) {
+        }
 }
 
 // ------------------------------------------------------------ host side
@@ -620,13 +843,17 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st) {
     if (((uintptr_t)a.x & 15) || a.x_id_stride % 16 || a.x_token_stride % 16) return 0;
     if (((uintptr_t)a.dst & 3) || a.dst_id_stride % 4 || a.dst_token_stride % 4) return 0;
 
-    const int m_tiles = a.rows / kM;
+    const int m_tiles = a.rows / kM, r_tiles16 = a.rows / 16;
     const long long max_tasks = (n_pairs / kMaxN + std::min<long long>(n_pairs, a.ex.n_experts) + 1) * m_tiles;
+    const long long max_mtasks = std::min<long long>(n_pairs, a.ex.n_experts) * r_tiles16;
+    const long long n_xrows = (long long)a.n_tokens * a.x_rows;
     auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t b_counts = up256((size_t)a.ex.n_experts * 4), b_cursor = b_counts;
     const size_t b_tasks = up256((size_t)max_tasks * sizeof(Task)), b_ntasks = 256;
+    const size_t b_mtasks = up256((size_t)max_mtasks * sizeof(Task));
     const size_t b_order = up256((size_t)n_pairs * 4), b_pairs = up256((size_t)n_pairs * sizeof(PairInfo));
-    const size_t need = b_counts + b_cursor + b_tasks + b_ntasks + b_order + b_pairs;
+    const size_t b_xh = up256((size_t)n_xrows * a.k * 2), b_xexp = up256((size_t)n_xrows * 4);
+    const size_t need = b_counts + b_cursor + b_tasks + b_ntasks + b_mtasks + b_order + b_pairs + 2 * b_xh + b_xexp;
     if (need > g_gs.cap) {
         if (g_gs.mem) {
             cudaDeviceSynchronize();   // no kernel of an earlier call may still use it
@@ -653,14 +880,29 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st) {
     g.counts = (int*)b;
     g.cursor = (int*)(b + b_counts);
     g.tasks = (Task*)(b + b_counts + b_cursor);
-    g.n_tasks = (int*)(b + b_counts + b_cursor + b_tasks);
-    g.order = (int*)(b + b_counts + b_cursor + b_tasks + b_ntasks);
-    g.pairs = (PairInfo*)(b + b_counts + b_cursor + b_tasks + b_ntasks + b_order);
+    uint8_t* q = b + b_counts + b_cursor + b_tasks;
+    g.n_tasks = (int*)q;
+    g.n_mtasks = (int*)(q + 16);
+    q += b_ntasks;
+    g.mtasks = (Task*)q;
+    q += b_mtasks;
+    g.order = (int*)q;
+    q += b_order;
+    g.pairs = (PairInfo*)q;
+    q += b_pairs;
+    __half* xh = (__half*)q;
+    __half* xl = (__half*)(q + b_xh);
+    int* xexp = (int*)(q + 2 * b_xh);
+    g.heavy = kGMaxGroups * 8;
+    g.r_tiles16 = r_tiles16;
     g.err = a.err;
 
     if (!g_attr_set) {
         if (!sb_cuda_ok(cudaFuncSetAttribute(k_prefill_iq3s, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total),
-                        "prefill smem attribute"))
+                        "prefill smem attribute") ||
+            !sb_cuda_ok(cudaFuncSetAttribute(k_group_mma_iq3s, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             MmaSmem::total),
+                        "grouped mma smem attribute"))
             return -1;
         int dev = 0, sms = 0;
         cudaGetDevice(&dev);
@@ -688,7 +930,23 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st) {
     gp.n_tasks = g.n_tasks;
     gp.pairs = g.pairs;
     gp.err = a.err;
-    k_prefill_iq3s<<<g_grid, kThreads, Smem::total, st>>>(gp);
+    k_x_split<<<(int)std::min<long long>((n_xrows + 7) / 8, 148LL * 8), 256, 0, st>>>(
+        (const uint8_t*)a.x, a.x_id_stride, a.x_token_stride, a.x_rows, (int)n_xrows, a.k, xh, xl, xexp);
+    k_prefill_iq3s<<<g_grid, kThreads, Smem::total, st>>>(gp);   // experts with >= heavy pairs
+    MmaParams mp{};
+    mp.base = a.ex.base;
+    mp.expert_stride = a.ex.expert_stride;
+    mp.rb = (int)rb;
+    mp.k = a.k;
+    mp.tasks = g.mtasks;
+    mp.n_tasks = g.n_mtasks;
+    mp.pairs = g.pairs;
+    mp.xh = xh;
+    mp.xl = xl;
+    mp.xexp = xexp;
+    mp.dst = (uint8_t*)a.dst;
+    mp.err = a.err;
+    k_group_mma_iq3s<<<g_grid, kGW * 32, MmaSmem::total, st>>>(mp);   // the rest
     sb_timing_end(tslot, st);
     return sb_cuda_ok(cudaGetLastError(), "prefill launch") ? 1 : -1;
 }

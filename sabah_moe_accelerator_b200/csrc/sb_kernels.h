@@ -71,7 +71,10 @@ bool sb_qt_supported(int qt);
 int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st);
 // grouped tcgen05 path for many (token, slot) pairs on a device-resident bank
 // (sb_prefill_iq3s.cu); same return convention
-int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st);
+int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force = false);
+// the fused block as grouped gate / up / down calls + SwiGLU + combine, for
+// many (token, slot) pairs on device-resident banks; same return convention
+int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st);
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);
 // After a device error: the fused block's cross-CTA arrival counters may have
 // been left mid-count by a kernel that gave up; the next call clears them.

@@ -511,6 +511,8 @@ int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
 
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !fast_path_enabled()) return 0;
+    const int grouped = sb_block_iq3s_grouped(a, st);   // many (token, slot) pairs
+    if (grouped != 0) return grouped;
     int wpt_g, gpw_g, wpt_d, gpw_d;
     if (!plan_groups(a.d_model, wpt_g, gpw_g) || !plan_groups(a.ff, wpt_d, gpw_d)) return 0;
     if (a.ff % 16 || a.d_model % 16) return 0;

@@ -481,8 +481,9 @@ struct GroupParams {
     int* cursor;      // [n_experts]
     Task* tasks;      // tcgen05 tasks: experts with >= heavy pairs
     int* n_tasks;
-    Task* mtasks;     // register-decode tasks: (expert, 16-row tile) of experts with < heavy pairs
-    int* n_mtasks;
+    Task* mtasks;     // register-decode experts (< heavy pairs): {expert, -, first pair, pairs}; a task
+                      // is (entry, 16-row tile), task index = entry * r_tiles16 + tile
+    int* n_mtasks;    // entries * r_tiles16
     int heavy, r_tiles16;
     int* order;       // [pairs] pair index in grouped order
     PairInfo* pairs;  // [pairs] grouped order
@@ -521,7 +522,7 @@ __global__ void k_group_plan(const GroupParams g) {
         const int ce = g.counts[e];
         c += ce;
         if (ce >= g.heavy) tc += (ce + kMaxN - 1) / kMaxN * g.m_tiles;
-        else if (ce > 0) mc += g.r_tiles16;
+        else if (ce > 0) mc += 1;
     }
     s_sum[threadIdx.x] = c;
     s_tsum[threadIdx.x] = tc;
@@ -545,13 +546,13 @@ __global__ void k_group_plan(const GroupParams g) {
             for (int n0 = 0; n0 < ce; n0 += kMaxN)
                 for (int mt = 0; mt < g.m_tiles; ++mt) g.tasks[tpos++] = Task{e, mt, pos + n0, min(kMaxN, ce - n0)};
         } else if (ce > 0) {
-            for (int rt = 0; rt < g.r_tiles16; ++rt) g.mtasks[mpos++] = Task{e, rt, pos, ce};
+            g.mtasks[mpos++] = Task{e, 0, pos, ce};
         }
         pos += ce;
     }
     if (threadIdx.x == 1023) {
         *g.n_tasks = s_tsum[1023];
-        *g.n_mtasks = s_msum[1023];
+        *g.n_mtasks = s_msum[1023] * g.r_tiles16;
     }
 }
 
@@ -637,7 +638,7 @@ __global__ void k_x_split(const uint8_t* x, size_t x_id_stride, size_t x_token_s
 constexpr int kGW = 12;                      // warps per CTA
 constexpr int kGTile = 16 * 880;             // a 16-row tile at k <= 2048
 constexpr int kGRep = 8;                     // grid-table replicas
-constexpr int kGMaxGroups = 8;               // pairs per task < 64
+constexpr int kGMaxGroups = 4;               // pairs per task < 32 (more go to the tcgen05 kernel)
 
 struct MmaSmem {
     static constexpr int grid = 0;                          // [512][kGRep] u32
@@ -651,7 +652,7 @@ static_assert(MmaSmem::tiles % 16 == 0 && kGTile % 16 == 0, "bulk-copy alignment
 struct MmaParams {
     const uint8_t* base;
     size_t expert_stride;
-    int rb, k;
+    int rb, k, r_tiles16;
     const Task* tasks;
     const int* n_tasks;
     const PairInfo* pairs;
@@ -692,8 +693,14 @@ __global__ void __launch_bounds__(kGW * 32, 1) k_group_mma_iq3s(const MmaParams 
     const uint32_t grep = (uint32_t)(lane & (kGRep - 1));
     uint32_t phase = 0;
     bool failed = false;
+    // task ti = (expert entry ti / r_tiles16, 16-row tile ti % r_tiles16)
+    auto task_at = [&](int ti) {
+        Task t = p.tasks[ti / p.r_tiles16];
+        t.mt = ti % p.r_tiles16;
+        return t;
+    };
     for (int ti = blockIdx.x * kGW + warp; ti < n_tasks; ti += stride) {
-        const Task t = p.tasks[ti];
+        const Task t = task_at(ti);
         if (lane == 0) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // earlier reads of the buffer
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
@@ -702,7 +709,7 @@ __global__ void __launch_bounds__(kGW * 32, 1) k_group_mma_iq3s(const MmaParams 
                          "l"(p.base + (size_t)t.expert * p.expert_stride + (size_t)t.mt * bytes), "r"(bytes), "r"(bar)
                          : "memory");
             if (ti + stride < n_tasks) {   // the next task's tile, into L2 meanwhile
-                const Task tn = p.tasks[ti + stride];
+                const Task tn = task_at(ti + stride);
                 asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
                                  p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * bytes),
                              "r"(bytes)
@@ -733,7 +740,26 @@ __global__ void __launch_bounds__(kGW * 32, 1) k_group_mma_iq3s(const MmaParams 
         float acc[kGMaxGroups][4];
 #pragma unroll
         for (int gr = 0; gr < kGMaxGroups; ++gr) acc[gr][0] = acc[gr][1] = acc[gr][2] = acc[gr][3] = 0.f;
+        // B fragments (hi, lo) of sub-block sb for each group; those of sb + 1
+        // are loaded while sb is multiplied
+        uint2 bh[kGMaxGroups][2], bl[kGMaxGroups][2];
+        auto load_b = [&](int sb, uint2 (&h)[kGMaxGroups][2], uint2 (&l)[kGMaxGroups][2]) {
+#pragma unroll
+            for (int gr = 0; gr < kGMaxGroups; ++gr)
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    h[gr][q] = l[gr][q] = make_uint2(0, 0);
+                    if (gr < ng && xr[gr] >= 0) {
+                        const size_t off = (size_t)xr[gr] * p.k + 32 * sb + 16 * q + 4 * c;
+                        h[gr][q] = __ldg((const uint2*)(p.xh + off));
+                        l[gr][q] = __ldg((const uint2*)(p.xl + off));
+                    }
+                }
+        };
+        load_b(0, bh, bl);
         for (int sb = 0; sb < p.k / 32; ++sb) {
+            uint2 nh[kGMaxGroups][2], nl[kGMaxGroups][2];
+            if (sb + 1 < p.k / 32) load_b(sb + 1, nh, nl);
             const int j = sb >> 3, ib = sb & 7;
             uint32_t a[2][2][2];   // [k16 half q][row h][reg]
             float db[2];
@@ -758,26 +784,24 @@ __global__ void __launch_bounds__(kGW * 32, 1) k_group_mma_iq3s(const MmaParams 
 #pragma unroll
             for (int gr = 0; gr < kGMaxGroups; ++gr) {
                 if (gr >= ng) break;
-                uint2 bh[2] = {make_uint2(0, 0), make_uint2(0, 0)}, bl[2] = {make_uint2(0, 0), make_uint2(0, 0)};
-                if (xr[gr] >= 0) {
-#pragma unroll
-                    for (int q = 0; q < 2; ++q) {
-                        const size_t off = (size_t)xr[gr] * p.k + 32 * sb + 16 * q + 4 * c;
-                        bh[q] = __ldg((const uint2*)(p.xh + off));
-                        bl[q] = __ldg((const uint2*)(p.xl + off));
-                    }
-                }
                 float dd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
-                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bh[q].x, bh[q].y);
-                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bl[q].x, bl[q].y);
+                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bh[gr][q].x, bh[gr][q].y);
+                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bl[gr][q].x, bl[gr][q].y);
                 }
                 acc[gr][0] = fmaf(db[0], dd[0], acc[gr][0]);
                 acc[gr][1] = fmaf(db[0], dd[1], acc[gr][1]);
                 acc[gr][2] = fmaf(db[1], dd[2], acc[gr][2]);
                 acc[gr][3] = fmaf(db[1], dd[3], acc[gr][3]);
             }
+#pragma unroll
+            for (int gr = 0; gr < kGMaxGroups; ++gr)
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    bh[gr][q] = nh[gr][q];
+                    bl[gr][q] = nl[gr][q];
+                }
         }
         // D: (row g, pair 2c), (row g, pair 2c + 1), (row g + 8, pair 2c), (row g + 8, pair 2c + 1)
 #pragma unroll
@@ -833,10 +857,10 @@ int sb_prefill_min_pairs() {
     return v;
 }
 
-int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st) {
+int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force) {
     if (a.qt != SB_IQ3_S || !prefill_enabled() || a.ex.ptrs) return 0;
     const long long n_pairs = (long long)a.n_ids * a.n_tokens;
-    if (n_pairs < sb_prefill_min_pairs() || n_pairs > (1 << 24)) return 0;
+    if ((!force && n_pairs < sb_prefill_min_pairs()) || n_pairs < 1 || n_pairs > (1 << 24)) return 0;
     if (a.k % 256 || a.k > 2048 || a.rows % kM || a.ex.n_experts < 1 || a.ex.n_experts > 65536) return 0;
     const size_t rb = sb_row_bytes_of(SB_IQ3_S, a.k);
     if (a.row_stride != rb || ((uintptr_t)a.ex.base & 15) || a.ex.expert_stride % 16 || (kM * rb) % 16) return 0;
@@ -845,7 +869,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st) {
 
     const int m_tiles = a.rows / kM, r_tiles16 = a.rows / 16;
     const long long max_tasks = (n_pairs / kMaxN + std::min<long long>(n_pairs, a.ex.n_experts) + 1) * m_tiles;
-    const long long max_mtasks = std::min<long long>(n_pairs, a.ex.n_experts) * r_tiles16;
+    const long long max_mtasks = std::min<long long>(n_pairs, a.ex.n_experts);
     const long long n_xrows = (long long)a.n_tokens * a.x_rows;
     auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t b_counts = up256((size_t)a.ex.n_experts * 4), b_cursor = b_counts;
@@ -938,6 +962,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st) {
     mp.expert_stride = a.ex.expert_stride;
     mp.rb = (int)rb;
     mp.k = a.k;
+    mp.r_tiles16 = r_tiles16;
     mp.tasks = g.mtasks;
     mp.n_tasks = g.n_mtasks;
     mp.pairs = g.pairs;
@@ -949,4 +974,116 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st) {
     k_group_mma_iq3s<<<g_grid, kGW * 32, MmaSmem::total, st>>>(mp);   // the rest
     sb_timing_end(tslot, st);
     return sb_cuda_ok(cudaGetLastError(), "prefill launch") ? 1 : -1;
+}
+
+// ------------------------------------------------------------ the fused block, grouped
+namespace {
+
+// h = silu(g) * u, elementwise
+__global__ void k_swiglu(const float* g, const float* u, float* h, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float gv = g[i];
+        h[i] = gv / (1.f + expf(-gv)) * u[i];
+    }
+}
+
+// out[t][i] = (accumulate ? out[t][i] : 0) + sum_e w[t][e] * y[t][e][i], slots in order
+__global__ void k_combine(const float* y, const float* w, float* out, int n_tokens, int n_used, int d_model,
+                          int accumulate) {
+    const long long n = (long long)n_tokens * d_model;
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < n; q += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(q / d_model), i = (int)(q % d_model);
+        float tot = 0.f;
+        for (int e = 0; e < n_used; ++e)
+            tot += w[(size_t)t * n_used + e] * y[((size_t)t * n_used + e) * d_model + i];
+        out[q] = accumulate ? out[q] + tot : tot;
+    }
+}
+
+struct BlockGroupedScratch {
+    float* mem = nullptr;
+    size_t cap = 0;   // floats
+};
+BlockGroupedScratch g_bgs;
+
+// Below this many (token, slot) pairs the fused block keeps its per-pair
+// kernels: with uniform routing most experts get one or two pairs, and the
+// per-pair pipeline streams a tile faster than the grouped kernels decode it.
+int block_grouped_min() {
+    static int v = -1;
+    if (v < 0) {
+        const char* s = std::getenv("SABAH_IQ3S_BLOCK_GROUPED_MIN");
+        v = s && *s ? std::max(1, std::atoi(s)) : 1024;
+    }
+    return v;
+}
+
+}  // namespace
+
+int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st) {
+    if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !prefill_enabled()) return 0;
+    const long long slots = (long long)a.n_tokens * a.n_used;
+    if (slots < block_grouped_min() || slots > (1 << 22)) return 0;
+    if (a.gate.ptrs || a.up.ptrs || a.down.ptrs) return 0;
+    if (a.d_model % 256 || a.ff % 256 || a.d_model > 2048 || a.ff > 2048 || a.d_model % kM || a.ff % kM) return 0;
+    for (const sb_experts* e : {&a.gate, &a.up, &a.down})
+        if (((uintptr_t)e->base & 15) || e->expert_stride % 16) return 0;
+    if (((uintptr_t)a.x & 15) || ((uintptr_t)a.h & 15) || ((uintptr_t)a.out & 3)) return 0;
+
+    const size_t need = (size_t)slots * (2 * a.ff + a.d_model);
+    if (need > g_bgs.cap) {
+        if (g_bgs.mem) {
+            cudaDeviceSynchronize();   // no kernel of an earlier call may still use it
+            cudaFree(g_bgs.mem);
+        }
+        g_bgs = BlockGroupedScratch{};
+        if (!sb_cuda_ok(cudaMalloc(&g_bgs.mem, need * sizeof(float)), "grouped block scratch")) return -1;
+        g_bgs.cap = need;
+    }
+    float* gout = g_bgs.mem;
+    float* uout = gout + slots * a.ff;
+    float* dout = uout + slots * a.ff;
+
+    sb_mmid_args m{};
+    m.row_stride = sb_row_bytes_of(SB_IQ3_S, a.d_model);
+    m.x = a.x;
+    m.x_id_stride = (size_t)a.d_model * 4;
+    m.x_rows = 1;
+    m.x_token_stride = (size_t)a.d_model * 4;
+    m.n_ids = a.n_used;
+    m.n_tokens = a.n_tokens;
+    m.dst_id_stride = (size_t)a.ff * 4;
+    m.dst_token_stride = (size_t)a.n_used * a.ff * 4;
+    m.rows = a.ff;
+    m.k = a.d_model;
+    m.qt = SB_IQ3_S;
+    m.err = a.err;
+    m.ex = a.gate;
+    m.dst = gout;
+    if (sb_try_mmid_iq3s_grouped(m, st, true) != 1) return -1;
+    m.ex = a.up;
+    m.dst = uout;
+    if (sb_try_mmid_iq3s_grouped(m, st, true) != 1) return -1;
+    const long long nh = slots * a.ff;
+    const int tslot = sb_timing_begin("block_grouped_elementwise", st);
+    k_swiglu<<<(int)std::min<long long>((nh + 255) / 256, 148LL * 8), 256, 0, st>>>(gout, uout, a.h, nh);
+    sb_timing_end(tslot, st);
+    m.ex = a.down;
+    m.row_stride = sb_row_bytes_of(SB_IQ3_S, a.ff);
+    m.x = a.h;
+    m.x_id_stride = (size_t)a.ff * 4;
+    m.x_rows = a.n_used;
+    m.x_token_stride = (size_t)a.n_used * a.ff * 4;
+    m.dst = dout;
+    m.dst_id_stride = (size_t)a.d_model * 4;
+    m.dst_token_stride = (size_t)a.n_used * a.d_model * 4;
+    m.rows = a.d_model;
+    m.k = a.ff;
+    if (sb_try_mmid_iq3s_grouped(m, st, true) != 1) return -1;
+    const long long no = (long long)a.n_tokens * a.d_model;
+    const int tslot2 = sb_timing_begin("block_grouped_elementwise", st);
+    k_combine<<<(int)std::min<long long>((no + 255) / 256, 148LL * 8), 256, 0, st>>>(dout, a.w, a.out, a.n_tokens,
+                                                                                     a.n_used, a.d_model, a.accumulate);
+    sb_timing_end(tslot2, st);
+    return sb_cuda_ok(cudaGetLastError(), "grouped block launch") ? 1 : -1;
 }

@@ -109,3 +109,33 @@ def test_block_ids_shape_changes(gpu_rt, orc):
                                      d_model, ff, qt, qt, qt)
             r = orc.rel_l2(got[t], want)
             assert r <= TOL and r <= TIGHT, (case, T, t, r)
+
+
+@pytest.mark.parametrize("T", [104, 128])
+def test_block_ids_grouped_path(gpu_rt, orc, T):
+    """T x top-10 >= 1024 (token, slot) pairs: the block runs as grouped gate / up
+    / down MUL_MAT_IDs + SwiGLU + combine; against fp64 (sampled tokens), then
+    with accumulate."""
+    from sabah_moe_accelerator_b200 import ops
+    d_model, ff, E, K, qt = 2048, 768, 24, 10, 21
+    gate = ops.synth_rows(E * ff, d_model, qt, seed=61, sigma=0.02)
+    up = ops.synth_rows(E * ff, d_model, qt, seed=62, sigma=0.02)
+    down = ops.synth_rows(E * d_model, ff, qt, seed=63, sigma=0.02)
+    rng = np.random.default_rng(400 + T)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, K)).astype(np.float32)
+    w /= w.sum(1, keepdims=True)
+    x = rng.standard_normal((T, d_model)).astype(np.float32)
+    ids_d, w_d, x_d = torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()
+    out = ops.moe_block_ids(gate, up, down, ids_d, w_d, x_d, d_model, ff, E, qt, qt, qt)
+    got = out.cpu().numpy()
+    g, u, d = gate.cpu().numpy(), up.cpu().numpy(), down.cpu().numpy()
+    sample = [0, 1, T // 2, T - 1]
+    want = np.stack([orc.moe_block_f64(g.reshape(E, -1), u.reshape(E, -1), d.reshape(E, -1), ids[t], w[t], x[t],
+                                       d_model, ff, qt, qt, qt) for t in sample])
+    for j, t in enumerate(sample):
+        r = orc.rel_l2(got[t], want[j])
+        assert r <= TOL and r <= TIGHT, (t, r)
+    ops.moe_block_ids(gate, up, down, ids_d, w_d, x_d, d_model, ff, E, qt, qt, qt, out=out, accumulate=True)
+    torch.cuda.synchronize()
+    assert orc.rel_l2(out.cpu().numpy(), 2 * got) <= TIGHT

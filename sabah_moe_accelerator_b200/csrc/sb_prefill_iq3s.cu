@@ -482,9 +482,9 @@ struct GroupParams {
     Task* tasks;      // tcgen05 tasks: experts with >= heavy pairs
     int* n_tasks;
     Task* mtasks;     // register-decode experts (< heavy pairs): {expert, -, first pair, pairs}; a task
-                      // is (entry, 16-row tile), task index = entry * r_tiles16 + tile
-    int* n_mtasks;    // entries * r_tiles16
-    int heavy, r_tiles16;
+                      // is (entry, 128-row block), task index = entry * m_tiles + block
+    int* n_mtasks;    // entries * m_tiles
+    int heavy;
     int* order;       // [pairs] pair index in grouped order
     PairInfo* pairs;  // [pairs] grouped order
     int* err;
@@ -552,7 +552,7 @@ __global__ void k_group_plan(const GroupParams g) {
     }
     if (threadIdx.x == 1023) {
         *g.n_tasks = s_tsum[1023];
-        *g.n_mtasks = s_msum[1023] * g.r_tiles16;
+        *g.n_mtasks = s_msum[1023] * g.m_tiles;
     }
 }
 
@@ -626,35 +626,42 @@ __global__ void k_x_split(const uint8_t* x, size_t x_id_stride, size_t x_token_s
 }
 
 // ------------------------------------------------------------ register-decode grouped kernel
-// For experts with few pairs. A warp owns a task (expert, 16-row tile, all of
-// the expert's n < heavy pairs): the tile lands in the warp's shared-memory
-// buffer by one bulk copy; per IQ3_S sub-block the warp decodes its A
-// fragments once (mma.sync m16n8k16 layout; the MMA's k slots {2c, 2c+1,
-// 2c+8, 2c+9} are mapped to the 4 weights of grid entry c, so one grid lookup
-// gives a thread its fragment, placed as fp16 subnormals b * 2^-24 with their
-// signs) and multiplies them with each group of 8 pairs' x (fp16 hi and lo
-// parts, split once per x row); the sub-block's scale is applied to the
-// group's fp32 partial sums.
-constexpr int kGW = 12;                      // warps per CTA
+// For experts with at most 8 routed pairs. A CTA task is (expert, 128-row
+// block): the producer warp bulk-copies the pairs' x rows (fp16 hi and lo
+// parts, split once per x row) and one 16-row weight tile per consumer warp
+// into shared memory; each of the 8 consumer warps then walks the IQ3_S
+// sub-blocks of its tile, decodes its A fragments once (mma.sync m16n8k16;
+// the MMA's k slots {2c, 2c+1, 2c+8, 2c+9} are mapped to the 4 weights of grid
+// entry c, placed as fp16 subnormals b * 2^-24 with their signs) and multiplies
+// them with the pairs' x (the 8 pairs are the MMA's 8 columns); the sub-block's
+// scale is applied to the fp32 partial sums. x and weights come from shared
+// memory, so the K loop never waits on L2.
+constexpr int kGW = 8;                       // consumer warps (16 rows each: one 128-row block)
+constexpr int kGThreads = (kGW + 1) * 32;    // + the producer warp
 constexpr int kGTile = 16 * 880;             // a 16-row tile at k <= 2048
 constexpr int kGRep = 8;                     // grid-table replicas
-constexpr int kGMaxGroups = 4;               // pairs per task < 32 (more go to the tcgen05 kernel)
+constexpr int kGMaxPairs = 8;                // pairs per expert on this kernel (more go to tcgen05)
+constexpr int kGXRow = 2048 * 2 + 32;        // bytes per staged x row (fp16, padded against bank conflicts)
 
 struct MmaSmem {
-    static constexpr int grid = 0;                          // [512][kGRep] u32
-    static constexpr int tiles = grid + 512 * kGRep * 4;    // [kGW][kGTile]
-    static constexpr int bars = tiles + kGW * kGTile;       // [kGW]
-    static constexpr int total = bars + kGW * 8;
+    static constexpr int grid = 0;                                   // [512][kGRep] u32
+    static constexpr int xh = grid + 512 * kGRep * 4;                // [kGMaxPairs][kGXRow]
+    static constexpr int xl = xh + kGMaxPairs * kGXRow;              // [kGMaxPairs][kGXRow]
+    static constexpr int tiles = xl + kGMaxPairs * kGXRow;           // [kGW][kGTile]
+    static constexpr int bars = tiles + kGW * kGTile;                // xbar, free, tile[kGW]
+    static constexpr int total = bars + (2 + kGW) * 8;
 };
 static_assert(MmaSmem::total <= 227 * 1024, "shared memory budget");
-static_assert(MmaSmem::tiles % 16 == 0 && kGTile % 16 == 0, "bulk-copy alignment");
+static_assert(MmaSmem::xh % 16 == 0 && MmaSmem::xl % 16 == 0 && MmaSmem::tiles % 16 == 0 && kGXRow % 16 == 0 &&
+                  kGTile % 16 == 0,
+              "bulk-copy alignment");
 
 struct MmaParams {
     const uint8_t* base;
     size_t expert_stride;
-    int rb, k, r_tiles16;
-    const Task* tasks;
-    const int* n_tasks;
+    int rb, k, m_tiles;
+    const Task* tasks;            // {expert, -, first pair, pairs}
+    const int* n_tasks;           // entries * m_tiles
     const PairInfo* pairs;
     const __half* xh;
     const __half* xl;
@@ -670,96 +677,101 @@ __device__ inline void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(kGW * 32, 1) k_group_mma_iq3s(const MmaParams p) {
+__device__ inline void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, c = lane & 3;
     uint32_t* gtab = (uint32_t*)(smem + MmaSmem::grid);
-    uint8_t* tile = smem + MmaSmem::tiles + warp * kGTile;
-    const uint32_t bar = smem_u32(smem + MmaSmem::bars + warp * 8);
-    for (int e = threadIdx.x; e < 512; e += kGW * 32) {
+    const uint32_t xbar = smem_u32(smem + MmaSmem::bars), freebar = xbar + 8, tbar0 = xbar + 16;
+    volatile int* abort_flag = nullptr;
+    __shared__ int s_abort;
+    for (int e = threadIdx.x; e < 512; e += kGThreads) {
         const uint32_t w = sb_iq3s_grid[e];
 #pragma unroll
         for (int r = 0; r < kGRep; ++r) gtab[e * kGRep + r] = w;
     }
-    if (lane == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar));
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(xbar));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(freebar), "r"(kGW));
+        for (int w = 0; w < kGW; ++w) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tbar0 + 8 * w));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    abort_flag = &s_abort;
     const int n_tasks = *p.n_tasks;
-    const uint32_t bytes = (uint32_t)(16 * p.rb);
-    const int stride = gridDim.x * kGW;
-    const uint32_t grep = (uint32_t)(lane & (kGRep - 1));
-    uint32_t phase = 0;
-    bool failed = false;
-    // task ti = (expert entry ti / r_tiles16, 16-row tile ti % r_tiles16)
+    const uint32_t tile_bytes = (uint32_t)(16 * p.rb), xrow_bytes = (uint32_t)(p.k * 2);
     auto task_at = [&](int ti) {
-        Task t = p.tasks[ti / p.r_tiles16];
-        t.mt = ti % p.r_tiles16;
+        Task t = p.tasks[ti / p.m_tiles];
+        t.mt = ti % p.m_tiles;
         return t;
     };
-    for (int ti = blockIdx.x * kGW + warp; ti < n_tasks; ti += stride) {
-        const Task t = task_at(ti);
+
+    if (warp == kGW) {
+        // ---------------------------------------------------------- producer (lane 0)
         if (lane == 0) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // earlier reads of the buffer
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                             smem_u32(tile)),
-                         "l"(p.base + (size_t)t.expert * p.expert_stride + (size_t)t.mt * bytes), "r"(bytes), "r"(bar)
-                         : "memory");
-            if (ti + stride < n_tasks) {   // the next task's tile, into L2 meanwhile
-                const Task tn = task_at(ti + stride);
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
-                                 p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * bytes),
-                             "r"(bytes)
+            int i = 0, last = -1;
+            for (int ti = blockIdx.x; ti < n_tasks; ti += gridDim.x, ++i) {
+                // the consumers are done with the previous task's buffers
+                if (i > 0 && !mbar_wait(freebar, (i - 1) & 1, p.err, abort_flag)) break;
+                const Task t = task_at(ti);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
+                             "r"(2u * xrow_bytes * (uint32_t)t.n)
                              : "memory");
-            }
-        }
-        // this lane's pair in each group of 8: n = 8 * gr + g
-        const int ng = (t.n + 7) >> 3;
-        int xr[kGMaxGroups];
-#pragma unroll
-        for (int gr = 0; gr < kGMaxGroups; ++gr) {
-            const int n = 8 * gr + g;
-            xr[gr] = (gr < ng && n < t.n) ? p.pairs[t.n0 + n].xrow : -1;
-        }
-        bool ok = true;
-        {
-            long long it = 0;
-            while (!mbar_try_wait(bar, phase) && ++it < kSpinLimit) {
-            }
-            ok = it < kSpinLimit;
-        }
-        if (!__all_sync(0xffffffffu, ok)) {   // the copy of this phase is still outstanding
-            if (lane == 0 && p.err) atomicExch(p.err, SB_DERR_TIMEOUT);
-            failed = true;
-            break;
-        }
-        phase ^= 1;
-        float acc[kGMaxGroups][4];
-#pragma unroll
-        for (int gr = 0; gr < kGMaxGroups; ++gr) acc[gr][0] = acc[gr][1] = acc[gr][2] = acc[gr][3] = 0.f;
-        // B fragments (hi, lo) of sub-block sb for each group; those of sb + 1
-        // are loaded while sb is multiplied
-        uint2 bh[kGMaxGroups][2], bl[kGMaxGroups][2];
-        auto load_b = [&](int sb, uint2 (&h)[kGMaxGroups][2], uint2 (&l)[kGMaxGroups][2]) {
-#pragma unroll
-            for (int gr = 0; gr < kGMaxGroups; ++gr)
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    h[gr][q] = l[gr][q] = make_uint2(0, 0);
-                    if (gr < ng && xr[gr] >= 0) {
-                        const size_t off = (size_t)xr[gr] * p.k + 32 * sb + 16 * q + 4 * c;
-                        h[gr][q] = __ldg((const uint2*)(p.xh + off));
-                        l[gr][q] = __ldg((const uint2*)(p.xl + off));
-                    }
+                for (int j = 0; j < t.n; ++j) {
+                    const int xr = p.pairs[t.n0 + j].xrow;
+                    bulk_copy(smem_u32(smem + MmaSmem::xh + j * kGXRow), p.xh + (size_t)xr * p.k, xrow_bytes, xbar);
+                    bulk_copy(smem_u32(smem + MmaSmem::xl + j * kGXRow), p.xl + (size_t)xr * p.k, xrow_bytes, xbar);
                 }
-        };
-        load_b(0, bh, bl);
+                const uint8_t* blk = p.base + (size_t)t.expert * p.expert_stride + (size_t)t.mt * kGW * tile_bytes;
+                for (int w = 0; w < kGW; ++w) {
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tbar0 + 8 * w),
+                                 "r"(tile_bytes)
+                                 : "memory");
+                    bulk_copy(smem_u32(smem + MmaSmem::tiles + w * kGTile), blk + (size_t)w * tile_bytes, tile_bytes,
+                              tbar0 + 8 * w);
+                }
+                if (ti + (int)gridDim.x < n_tasks) {   // the next task's weights, into L2 meanwhile
+                    const Task tn = task_at(ti + gridDim.x);
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                                     p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * kGW * tile_bytes),
+                                 "r"(kGW * tile_bytes)
+                                 : "memory");
+                }
+                last = i;
+            }
+            // never leave with copies in flight: the last task's copies have landed
+            if (last >= 0) {
+                for (long long it = 0; it < kSpinLimit && !mbar_try_wait(xbar, last & 1); ++it) {
+                }
+                for (int w = 0; w < kGW; ++w)
+                    for (long long it = 0; it < kSpinLimit && !mbar_try_wait(tbar0 + 8 * w, last & 1); ++it) {
+                    }
+            }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------- consumers
+    const int g = lane >> 2, c = lane & 3;
+    const uint32_t grep = (uint32_t)(lane & (kGRep - 1));
+    const uint8_t* tile = smem + MmaSmem::tiles + warp * kGTile;
+    const uint8_t* xhs = smem + MmaSmem::xh + g * kGXRow;   // this lane's pair column g
+    const uint8_t* xls = smem + MmaSmem::xl + g * kGXRow;
+    int i = 0;
+    for (int ti = blockIdx.x; ti < n_tasks; ti += gridDim.x, ++i) {
+        const Task t = task_at(ti);
+        const bool ok = mbar_wait(xbar, i & 1, p.err, abort_flag) && mbar_wait(tbar0 + 8 * warp, i & 1, p.err, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const bool have = g < t.n;   // pair column g exists (else its B is zero)
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int sb = 0; sb < p.k / 32; ++sb) {
-            uint2 nh[kGMaxGroups][2], nl[kGMaxGroups][2];
-            if (sb + 1 < p.k / 32) load_b(sb + 1, nh, nl);
             const int j = sb >> 3, ib = sb & 7;
             uint32_t a[2][2][2];   // [k16 half q][row h][reg]
             float db[2];
@@ -781,49 +793,38 @@ __global__ void __launch_bounds__(kGW * 32, 1) k_group_mma_iq3s(const MmaParams 
                     a[q][h][1] = prmt(gw, Z, 0x7362);   // (w2, w3)
                 }
             }
+            float dd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int gr = 0; gr < kGMaxGroups; ++gr) {
-                if (gr >= ng) break;
-                float dd[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bh[gr][q].x, bh[gr][q].y);
-                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bl[gr][q].x, bl[gr][q].y);
+            for (int q = 0; q < 2; ++q) {
+                const int off = 2 * (32 * sb + 16 * q + 4 * c);
+                uint2 bh = make_uint2(0, 0), bl = make_uint2(0, 0);
+                if (have) {
+                    bh = *(const uint2*)(xhs + off);
+                    bl = *(const uint2*)(xls + off);
                 }
-                acc[gr][0] = fmaf(db[0], dd[0], acc[gr][0]);
-                acc[gr][1] = fmaf(db[0], dd[1], acc[gr][1]);
-                acc[gr][2] = fmaf(db[1], dd[2], acc[gr][2]);
-                acc[gr][3] = fmaf(db[1], dd[3], acc[gr][3]);
+                mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bh.x, bh.y);
+                mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bl.x, bl.y);
             }
-#pragma unroll
-            for (int gr = 0; gr < kGMaxGroups; ++gr)
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    bh[gr][q] = nh[gr][q];
-                    bl[gr][q] = nl[gr][q];
-                }
+            acc[0] = fmaf(db[0], dd[0], acc[0]);
+            acc[1] = fmaf(db[0], dd[1], acc[1]);
+            acc[2] = fmaf(db[1], dd[2], acc[2]);
+            acc[3] = fmaf(db[1], dd[3], acc[3]);
         }
         // D: (row g, pair 2c), (row g, pair 2c + 1), (row g + 8, pair 2c), (row g + 8, pair 2c + 1)
+        const int row0 = (t.mt * kGW + warp) * 16;
 #pragma unroll
-        for (int gr = 0; gr < kGMaxGroups; ++gr) {
-            if (gr >= ng) break;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int n = 8 * gr + 2 * c + u;
-                if (n >= t.n) continue;
-                const PairInfo pi = p.pairs[t.n0 + n];
-                float* d = (float*)(p.dst + pi.dst_off) + t.mt * 16;
-                const int ex = p.xexp[pi.xrow];
-                d[g] = ldexpf(acc[gr][u], -ex);
-                d[g + 8] = ldexpf(acc[gr][2 + u], -ex);
-            }
+        for (int u = 0; u < 2; ++u) {
+            const int n = 2 * c + u;
+            if (n >= t.n) continue;
+            const PairInfo pi = p.pairs[t.n0 + n];
+            float* d = (float*)(p.dst + pi.dst_off) + row0;
+            const int ex = p.xexp[pi.xrow];
+            d[g] = ldexpf(acc[u], -ex);
+            d[g + 8] = ldexpf(acc[2 + u], -ex);
         }
-        __syncwarp();   // every lane is done with the tile before the next copy overwrites it
+        __syncwarp();   // every lane is done with the buffers
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(freebar) : "memory");
     }
-    // never leave with a copy in flight
-    if (failed && lane == 0)
-        for (long long it = 0; it < kSpinLimit && !mbar_try_wait(bar, phase); ++it) {
-        }
 }
 
 // ------------------------------------------------------------ host side
@@ -867,7 +868,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
     if (((uintptr_t)a.x & 15) || a.x_id_stride % 16 || a.x_token_stride % 16) return 0;
     if (((uintptr_t)a.dst & 3) || a.dst_id_stride % 4 || a.dst_token_stride % 4) return 0;
 
-    const int m_tiles = a.rows / kM, r_tiles16 = a.rows / 16;
+    const int m_tiles = a.rows / kM;
     const long long max_tasks = (n_pairs / kMaxN + std::min<long long>(n_pairs, a.ex.n_experts) + 1) * m_tiles;
     const long long max_mtasks = std::min<long long>(n_pairs, a.ex.n_experts);
     const long long n_xrows = (long long)a.n_tokens * a.x_rows;
@@ -917,8 +918,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
     __half* xh = (__half*)q;
     __half* xl = (__half*)(q + b_xh);
     int* xexp = (int*)(q + 2 * b_xh);
-    g.heavy = kGMaxGroups * 8;
-    g.r_tiles16 = r_tiles16;
+    g.heavy = kGMaxPairs + 1;
     g.err = a.err;
 
     if (!g_attr_set) {
@@ -962,7 +962,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
     mp.expert_stride = a.ex.expert_stride;
     mp.rb = (int)rb;
     mp.k = a.k;
-    mp.r_tiles16 = r_tiles16;
+    mp.m_tiles = m_tiles;
     mp.tasks = g.mtasks;
     mp.n_tasks = g.n_mtasks;
     mp.pairs = g.pairs;
@@ -971,7 +971,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
     mp.xexp = xexp;
     mp.dst = (uint8_t*)a.dst;
     mp.err = a.err;
-    k_group_mma_iq3s<<<g_grid, kGW * 32, MmaSmem::total, st>>>(mp);   // the rest
+    k_group_mma_iq3s<<<g_grid, kGThreads, MmaSmem::total, st>>>(mp);   // the rest
     sb_timing_end(tslot, st);
     return sb_cuda_ok(cudaGetLastError(), "prefill launch") ? 1 : -1;
 }
@@ -1007,13 +1007,14 @@ struct BlockGroupedScratch {
 BlockGroupedScratch g_bgs;
 
 // Below this many (token, slot) pairs the fused block keeps its per-pair
-// kernels: with uniform routing most experts get one or two pairs, and the
-// per-pair pipeline streams a tile faster than the grouped kernels decode it.
+// kernels. Measured on B200 (2048 x 768 experts, 512 of them, uniform top-1
+// routing): per-pair costs ~1.8 us a pair, grouped ~250 us + ~0.75 us a pair;
+// they cross near 350 pairs.
 int block_grouped_min() {
     static int v = -1;
     if (v < 0) {
         const char* s = std::getenv("SABAH_IQ3S_BLOCK_GROUPED_MIN");
-        v = s && *s ? std::max(1, std::atoi(s)) : 1024;
+        v = s && *s ? std::max(1, std::atoi(s)) : 384;
     }
     return v;
 }

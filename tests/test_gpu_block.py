@@ -111,9 +111,9 @@ def test_block_ids_shape_changes(gpu_rt, orc):
             assert r <= TOL and r <= TIGHT, (case, T, t, r)
 
 
-@pytest.mark.parametrize("T", [104, 128])
+@pytest.mark.parametrize("T", [40, 104])
 def test_block_ids_grouped_path(gpu_rt, orc, T):
-    """T x top-10 >= 1024 (token, slot) pairs: the block runs as grouped gate / up
+    """T x top-10 >= 384 (token, slot) pairs: the block runs as grouped gate / up
     / down MUL_MAT_IDs + SwiGLU + combine; against fp64 (sampled tokens), then
     with accumulate."""
     from sabah_moe_accelerator_b200 import ops

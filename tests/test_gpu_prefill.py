@@ -88,3 +88,25 @@ def test_grouped_out_of_range_id(gpu_rt):
     o[7, 2] = 0.0
     assert np.isfinite(o).all()
     assert rt.lib().sabah_rt_device_error() == 1
+
+
+@pytest.mark.parametrize("skew", [0.0, 1.2])
+def test_grouped_light_and_mixed_experts(gpu_rt, orc, skew):
+    """Many experts with few pairs each (the register-decode path: at most 8
+    pairs per expert) and, with a Zipf-skewed routing, heavy experts beside
+    them (the tcgen05 path) in one call."""
+    from sabah_moe_accelerator_b200 import ops
+    rows, k, E, K, T = 256, 1024, 64, 8, 40   # 320 pairs, 5 per expert on average
+    bank, rb = _bank(E, rows, k, seed=int(skew * 10) + 5)
+    rng = np.random.default_rng(17)
+    p = 1.0 / np.arange(1, E + 1) ** skew
+    p /= p.sum()
+    ids = np.stack([rng.choice(E, K, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+    counts = np.bincount(ids.ravel(), minlength=E)
+    light = int(((counts > 0) & (counts <= 8)).sum())
+    assert light >= 40 and (skew == 0.0 or counts.max() > 8)
+    x = rng.standard_normal((T, 1, k)).astype(np.float32)
+    out = ops.mul_mat_id(bank, rows * rb, rb, torch.from_numpy(x).cuda(), torch.from_numpy(ids).cuda(),
+                         rows, k, E, QT).cpu().numpy()
+    want = orc.mmid_f64(bank.cpu().numpy(), rows * rb, rb, x, 1, ids, rows, k, E, QT)
+    _check(out, want)

@@ -4,8 +4,11 @@
 // With many tokens per call, MUL_MAT_ID is a grouped GEMM: expert e multiplies
 // its matrix W_e [rows][k] by the x rows of the n_e (token, slot) pairs routed
 // to it. The (token, slot) pairs are grouped by expert on the device (count,
-// scan, scatter), then a persistent kernel walks tasks (expert, 128-row tile,
-// up to 256 pairs):
+// scan, scatter). Experts with more than 8 pairs go to the tcgen05 kernel
+// below, which walks tasks (expert, 128-row tile, up to 128 pairs); experts
+// with 1-8 pairs go to a register-decode kernel (mma.sync, further down),
+// because a 128-wide MMA tile would be mostly padding for them. Both run in
+// one stream, back to back. In the tcgen05 kernel:
 //
 // * the tile's raw IQ3_S rows (128 x row bytes, contiguous in the bank) land in
 //   shared memory with one cp.async.bulk: every weight byte is read from HBM
@@ -37,10 +40,11 @@
 
 namespace {
 
-// Warp roles: warps 0-3 dequantise A (one thread per row) from the task's raw
-// tile in shared memory, warps 4-7 convert B (the pairs' x; one thread per
-// pair), warp 8 owns TMEM and issues the MMAs (lane 0). Warps 0-7 run the
-// epilogue. Stages move between them through full / empty mbarriers.
+// Warp roles: warps 0-7 (the producers) each slice dequantise A (thread t:
+// row t % 128, half the sub-block's grid entries) from the task's raw tile in
+// shared memory and convert B (the pairs' x, 8-wide chunks); warp 8 owns TMEM
+// and issues the MMAs (lane 0). Warps 0-7 run the epilogue. Stages move
+// between them through full / empty mbarriers.
 constexpr int kProducers = 256;                   // warps 0-7
 constexpr int kThreads = kProducers + 32;         // + the MMA warp
 constexpr int kM = 128;                           // rows per task (MMA M)

@@ -686,6 +686,185 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
     }
 
 
+# cfg 4: mixed Q4_K (gate, up) / Q6_K (down) decode, batch 4, Markov routing
+QT_Q4_K, QT_Q6_K = 12, 14
+MX_TOKENS, MX_SETS = 4, 4
+MX_GU_ROW = D_MODEL // 256 * 144               # 1152
+MX_D_ROW = FF // 256 * 210                     # 630
+MX_GU_EXPERT = FF * MX_GU_ROW                  # 884,736
+MX_D_EXPERT = D_MODEL * MX_D_ROW               # 1,290,240
+MX_METRIC = "MoE MUL_MAT_ID tokens/s (Q4_K gate/up + Q6_K down decode, batch 4, 48 x 512-expert bank resident)"
+MX_WORKLOAD = ("cfg4: Q4_K gate/up + Q6_K down decode, 4 tokens x 48 blocks, 512 experts/block, top-10, "
+               "Markov routing (p_keep 0.8), H2048 F768, 75.2 GB bank on 1 GPU")
+
+
+def markov_routing(n_sets: int, n_tok: int, layers: int, p_keep: float = 0.8, seed: int = 31):
+    """ids/w [n_sets][layers][n_tok][TOP_K]: token 0 draws TOP_K distinct experts;
+    each later token keeps the previous token's expert in a slot with p_keep,
+    else draws a fresh expert distinct from the token's others."""
+    ids = np.empty((n_sets, layers, n_tok, TOP_K), np.int32)
+    w = np.empty((n_sets, layers, n_tok, TOP_K), np.float32)
+    for s in range(n_sets):
+        rng = np.random.default_rng(seed + 1000 * s)
+        for L in range(layers):
+            prev = rng.choice(EXPERTS, TOP_K, replace=False)
+            for t in range(n_tok):
+                if t > 0:
+                    cur = prev.copy()
+                    for i in range(TOP_K):
+                        if rng.random() >= p_keep:
+                            while True:
+                                e = int(rng.integers(EXPERTS))
+                                if e not in cur:
+                                    break
+                            cur[i] = e
+                    prev = cur
+                ids[s, L, t] = prev
+                ww = rng.random(TOP_K) + 0.1
+                w[s, L, t] = (ww / ww.sum()).astype(np.float32)
+    return ids, w
+
+
+def run_mixed(args, rank: int, world: int, local_rank: int):
+    """cfg 4: 4 tokens through 48 Q4_K/Q6_K blocks per step, through
+    sabah_moe_decode on a device-resident bank."""
+    import torch
+    from sabah_moe_accelerator_b200 import ops, rt
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ops.init(local_rank)
+    L = rt.lib()
+    stream = torch.cuda.Stream(device=dev)
+    T = MX_TOKENS
+    layer_bytes = EXPERTS * (2 * MX_GU_EXPERT + MX_D_EXPERT)
+    bank = torch.empty(LAYERS * layer_bytes, dtype=torch.uint8, device=dev)
+    gate_p, up_p, down_p = [], [], []
+    with torch.cuda.stream(stream):
+        for Lr in range(LAYERS):
+            base = Lr * layer_bytes
+            for role, off, rows, k, qt, n in ((0, 0, FF, D_MODEL, QT_Q4_K, EXPERTS * MX_GU_EXPERT),
+                                              (1, EXPERTS * MX_GU_EXPERT, FF, D_MODEL, QT_Q4_K, EXPERTS * MX_GU_EXPERT),
+                                              (2, 2 * EXPERTS * MX_GU_EXPERT, D_MODEL, FF, QT_Q6_K,
+                                               EXPERTS * MX_D_EXPERT)):
+                view = bank[base + off: base + off + n]
+                ops.synth_rows(EXPERTS * rows, k, qt, seed=(30 + Lr) * 4 + role, sigma=0.02, out=view, stream=stream)
+                (gate_p, up_p, down_p)[role].append(view.data_ptr())
+    stream.synchronize()
+    ids_np, w_np = markov_routing(MX_SETS, T, LAYERS)
+    ids_d = torch.from_numpy(ids_np).to(dev)
+    w_d = torch.from_numpy(w_np).to(dev)
+    x0_np = np.random.default_rng(32).standard_normal((T, D_MODEL)).astype(np.float32)
+    x0_d = torch.from_numpy(x0_np).to(dev)
+    x_d = torch.empty_like(x0_d)
+    h_d = torch.empty((T, TOP_K, FF), dtype=torch.float32, device=dev)
+    c_arr = ctypes.c_void_p * LAYERS
+    G, U, D = c_arr(*gate_p), c_arr(*up_p), c_arr(*down_p)
+
+    def decode(ids_ptr, w_ptr, st):
+        rc = L.sabah_moe_decode(LAYERS, G, U, D, MX_GU_EXPERT, MX_D_EXPERT, EXPERTS, ids_ptr, w_ptr,
+                                x_d.data_ptr(), h_d.data_ptr(), D_MODEL, FF, TOP_K, T, QT_Q4_K, QT_Q4_K, QT_Q6_K,
+                                st.cuda_stream)
+        rt.check(rc, "sabah_moe_decode")
+
+    def step(s):
+        x_d.copy_(x0_d)
+        decode(ids_d[s].data_ptr(), w_d[s].data_ptr(), stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i % MX_SETS)
+    stream.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(args.steps):
+            step(i % MX_SETS)
+        t1.record(stream)
+    stream.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+
+    timing_steps = 2
+    L.sabah_rt_kernel_timing(1)
+    with torch.cuda.stream(stream):
+        for i in range(timing_steps):
+            step(i % MX_SETS)
+    stream.synchronize()
+    buf = ctypes.create_string_buffer(8192)
+    L.sabah_rt_kernel_times(buf, 8192)
+    L.sabah_rt_kernel_timing(0)
+    ktimes = json.loads(buf.value.decode())
+    launches_per_step = sum(v[0] for v in ktimes.values()) / timing_steps
+
+    # algorithmic bytes: each distinct routed expert of a block once, plus activations
+    distinct = np.array([[np.unique(ids_np[s, Lr]).size for Lr in range(LAYERS)] for s in range(MX_SETS)], np.float64)
+    d_mean = float(distinct.mean())
+    gu_bytes = d_mean * 2 * MX_GU_EXPERT + T * D_MODEL * 4 + T * TOP_K * FF * 4
+    dn_bytes = d_mean * MX_D_EXPERT + T * TOP_K * FF * 4 + 2 * T * D_MODEL * 4
+    step_bytes = LAYERS * (gu_bytes + dn_bytes)
+    kbytes = {"gate_up": gu_bytes, "down": dn_bytes, "decode": step_bytes}
+    dom_name, dom = max(ktimes.items(), key=lambda kv: kv[1][1])
+    family = "decode" if "decode" in dom_name else "gate_up" if "gate_up" in dom_name else "down"
+    avg_ms = dom[1] / dom[0]
+    peaks, peak_kind = measured_peaks()
+    achieved = kbytes[family] / (avg_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                "peak_kind": peak_kind, "bytes_per_launch": int(kbytes[family]),
+                "avg_launch_us": round(avg_ms * 1e3, 2),
+                "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)} for k, v in ktimes.items()}}
+
+    # e2e through the C ABI with host inputs and the result read back
+    x0_h = torch.from_numpy(x0_np).pin_memory()
+    ids_h = torch.from_numpy(ids_np).pin_memory()
+    w_h = torch.from_numpy(w_np).pin_memory()
+    out_h = torch.empty((T, D_MODEL), dtype=torch.float32).pin_memory()
+    ids_cur, w_cur = torch.empty_like(ids_d[0]), torch.empty_like(w_d[0])
+
+    def e2e_step(s):
+        x_d.copy_(x0_h, non_blocking=True)
+        ids_cur.copy_(ids_h[s], non_blocking=True)
+        w_cur.copy_(w_h[s], non_blocking=True)
+        decode(ids_cur.data_ptr(), w_cur.data_ptr(), stream)
+        out_h.copy_(x_d, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            e2e_step(i % MX_SETS)
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            e2e_step(i % MX_SETS)
+        e1.record(stream)
+    stream.synchronize()
+    e_ms = e0.elapsed_time(e1) / e2e_steps
+    assert np.isfinite(out_h.numpy()).all(), "non-finite decode output"
+    return {
+        "metric": MX_METRIC, "value": round(T * 1e3 / ms, 2), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (N(0,0.02) weights Q4_K/Q6_K-encoded on device, Markov routing, N(0,1) x)",
+        "config": {"workload": MX_WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+                   "top_k": TOP_K, "tokens_per_step": T, "distinct_experts_per_block": round(d_mean, 2),
+                   "l2": "inputs larger than L2: %.0f MB of distinct expert bytes per step, %d routing sets cycled"
+                         % (LAYERS * d_mean * (2 * MX_GU_EXPERT + MX_D_EXPERT) / 1e6, MX_SETS)},
+        "achieved_step_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+        "roofline": roofline,
+        "e2e": {"value": round(T * 1e3 / e_ms, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x0_h.numel() * 4 + ids_h[0].numel() * 4 + w_h[0].numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
+                "path": "sabah_moe_decode (C ABI), eager launches"},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "clocks": clk,
+    }
+
+
 def main():
     global LAYERS, BYTES_PER_TOKEN, WORKLOAD
     ap = argparse.ArgumentParser()
@@ -694,9 +873,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg5"],
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5"],
                     help="cfg2: the headline 1-token decode (replicas for N > 1); cfg3: 512-token prefill "
-                         "of one block; cfg5: expert-parallel bank")
+                         "of one block; cfg4: Q4_K/Q6_K batch-4 decode; cfg5: expert-parallel bank")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="blocks per token; fewer than 48 only for small profiling cases (not the benchmark)")
     args = ap.parse_args()
@@ -721,6 +900,8 @@ def main():
         res = run_ep(args, rank, world, local_rank)
     elif args.workload == "cfg3":
         res = run_prefill(args, rank, world, local_rank) if rank == 0 else None
+    elif args.workload == "cfg4":
+        res = run_mixed(args, rank, world, local_rank) if rank == 0 else None
     else:
         res = run_ours(args, rank, world, local_rank)
     if rank == 0 and res is not None:

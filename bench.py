@@ -866,7 +866,7 @@ def run_mixed(args, rank: int, world: int, local_rank: int):
 
 
 def main():
-    global LAYERS, BYTES_PER_TOKEN, WORKLOAD
+    global LAYERS, BYTES_PER_TOKEN, WORKLOAD, MX_WORKLOAD
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -883,6 +883,7 @@ def main():
         LAYERS = args.layers
         BYTES_PER_TOKEN = LAYERS * TOP_K * (2 * GU_EXPERT + D_EXPERT)
         WORKLOAD = "profiling case (not the benchmark): %d blocks of the cfg2 shape" % LAYERS
+        MX_WORKLOAD = "profiling case (not the benchmark): %d blocks of the cfg4 shape" % LAYERS
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

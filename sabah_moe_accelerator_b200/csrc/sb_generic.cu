@@ -207,6 +207,8 @@ int sb_launch_dequant(const void* src, float* dst, int qt, int n_rows, int row_e
 int sb_launch_block(const sb_block_args& a, cudaStream_t st) {
     const int taken = sb_try_block_iq3s(a, st);
     if (taken != 0) return taken > 0 ? 0 : -1;
+    const int small = sb_try_block_small(a, st);
+    if (small != 0) return small > 0 ? 0 : -1;
     dim3 g1((a.ff + kRowsPerCta - 1) / kRowsPerCta, a.n_used, a.n_tokens);
     bool ok;
     const int t1 = sb_timing_begin("gate_up_generic", st);

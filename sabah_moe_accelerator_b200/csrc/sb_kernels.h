@@ -76,6 +76,9 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force 
 // many (token, slot) pairs on device-resident banks; same return convention
 int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st);
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);
+// Q4_K / Q6_K fused block for 1-4 tokens on device banks, each distinct routed
+// expert decoded once per block (sb_small_kq.cu): 1 taken, 0 not covered, -1 error
+int sb_try_block_small(const sb_block_args& a, cudaStream_t st);
 // After a device error: the fused block's cross-CTA arrival counters may have
 // been left mid-count by a kernel that gave up; the next call clears them.
 void sb_block_scratch_invalidate();

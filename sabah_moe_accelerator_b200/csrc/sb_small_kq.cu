@@ -30,9 +30,9 @@
 //   (max into [2^13, 2^14)), so products keep ~22 bits, fp32-grade.
 //
 // Pipeline: a producer warp (8 issuing lanes) streams tiles into an 8-stage
-// ring with cp.async.bulk and mbarriers; 8 consumer warps split an item's
-// k-units (all 8 for k = 2048, 4 for k = 768) and the last one to finish sums
-// the partial rows in fixed order. Q4_K rows at k = 2048 are 1152 B, a
+// ring with cp.async.bulk and mbarriers; 16 consumer warps take an item's
+// super-blocks, one each (8 warps per item at k = 2048, 3 at k = 768), and the
+// last one to finish sums the partial rows in fixed order. Q4_K rows at k = 2048 are 1152 B, a
 // multiple of 128, so the 8 rows an MMA reads at one offset would share banks;
 // such tiles are copied row by row into a 1168-byte stride instead. Every wait
 // is bounded; a CTA that gives up records SB_DERR_TIMEOUT and drains its copies.
@@ -107,6 +107,9 @@ struct SmallParams {
 };
 
 __device__ inline void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
+// the routing plan is ready: the producer warp arrives, the consumers wait
+__device__ inline void plan_arrive() { asm volatile("bar.arrive 2, %0;" ::"n"(kThreads) : "memory"); }
+__device__ inline void plan_wait() { asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory"); }
 
 __device__ inline uint32_t lds32(const uint8_t* p) { return *(const uint32_t*)p; }
 __device__ inline uint32_t lds16x2(const uint8_t* p) {   // 4 bytes at a 2-byte-aligned address
@@ -282,113 +285,128 @@ __device__ void stage_rows(uint8_t* smem, int n_rows, int k, Src src) {
     consumers_sync();
 }
 
-// ------------------------------------------------------------ decode units
-// One k-unit (64 weights) of rows g and g + 8 of a tile, times this lane's B
-// column; acc[h] collects row g + 8h of column pair c. bh / bl: this lane's
-// column in the hi / lo B rows (byte address of element 0); sums: the scaled
-// 16-element sums of column c.
+// ------------------------------------------------------------ decode
+// One super-block (256 weights) of rows g and g + 8 of a tile, times this
+// lane's B column; acc[h] collects row g + 8h of column pair c. bcol: this
+// lane's column in the hi or lo B rows (byte address of element 0); sums: the
+// scaled 16-element sums of column c. The super-block header is read once and
+// its 4 k-units of 64 weights are unrolled, so every scale index is a constant.
 template <int QT>
 struct KQ;
 
 template <>
 struct KQ<SB_Q4_K> {
-    // unit u: super-block u / 4, quant bytes 32 * (u % 4) .. + 31: low nibbles
-    // are sub-block 2i, high nibbles sub-block 2i + 1 (i = u % 4)
-    __device__ static void unit(const uint8_t* tile, int rs, int u, int g, int c, const uint8_t* bcol, bool have,
-                                const float* sums, float (&acc)[2]) {
-        const int sbk = u >> 2, i = u & 3;
-        uint32_t w[2][2];
-        float s0[2][2], off[2][2];
+    // k-unit i: quant bytes 32i .. 32i + 31; low nibbles are sub-block 2i,
+    // high nibbles sub-block 2i + 1
+    __device__ static void superblock(const uint8_t* tile, int rs, int sbk, int g, int c, const uint8_t* bcol,
+                                      bool have, const float* sums, float (&acc)[2]) {
+        const uint8_t* b[2] = {tile + (size_t)g * rs + sbk * 144, tile + (size_t)(g + 8) * rs + sbk * 144};
+        float d[2], dmin[2];
+        uint32_t W[2][3];   // the 12 scale bytes (ggml's get_scale_min_k4 packing, as sb_kscale)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const uint8_t* b = tile + (size_t)(g + 8 * h) * rs + sbk * 144;
-            w[h][0] = lds32(b + 16 + 32 * i + 4 * c);
-            w[h][1] = lds32(b + 16 + 32 * i + 16 + 4 * c);
-            const uint32_t dm = lds32(b);
-            const float d = __half2float(__ushort_as_half((unsigned short)(dm & 0xFFFF)));
-            const float dmin = __half2float(__ushort_as_half((unsigned short)(dm >> 16)));
-            // the 12 scale bytes as 3 words: 6-bit scale and min of sub-block j
-            // (ggml's get_scale_min_k4 packing, as sb_kscale)
-            const uint32_t W0 = lds32(b + 4), W1 = lds32(b + 8), W2 = lds32(b + 12);
-#pragma unroll
-            for (int s = 0; s < 2; ++s) {
-                const int j = 2 * i + s;
-                int sc, mn;
-                if (j < 4) {
-                    sc = (W0 >> (8 * j)) & 63;
-                    mn = (W1 >> (8 * j)) & 63;
-                } else {
-                    const int jj = j - 4;
-                    const uint32_t b8 = (W2 >> (8 * jj)) & 0xFF;   // byte j + 4
-                    sc = (b8 & 15) | (((W0 >> (8 * jj + 6)) & 3) << 4);
-                    mn = (b8 >> 4) | (((W1 >> (8 * jj + 6)) & 3) << 4);
-                }
-                s0[h][s] = sb_mul(d, (float)sc) * 16777216.0f;   // 2^24 undoes the subnormal encoding
-                off[h][s] = -sb_mul(dmin, (float)mn);
-            }
+            const uint32_t dm = lds32(b[h]);
+            d[h] = __half2float(__ushort_as_half((unsigned short)(dm & 0xFFFF)));
+            dmin[h] = __half2float(__ushort_as_half((unsigned short)(dm >> 16)));
+            W[h][0] = lds32(b[h] + 4);
+            W[h][1] = lds32(b[h] + 8);
+            W[h][2] = lds32(b[h] + 12);
         }
-        const int e0 = sbk * 256 + 64 * i;   // first element of sub-block 2i
+        const uint8_t* bx = bcol + 2 * (sbk * 256 + 4 * c);
+        const float* sx = sums + sbk * 16;
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {        // sub-block 2i + s
-            float dd[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int i = 0; i < 4; ++i) {
+            uint32_t w[2][2];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t qg = w[0][half], q8 = w[1][half];
-                qg = s ? (qg >> 4) & 0x0F0F0F0Fu : qg & 0x0F0F0F0Fu;
-                q8 = s ? (q8 >> 4) & 0x0F0F0F0Fu : q8 & 0x0F0F0F0Fu;
-                uint32_t a0, a2, a1, a3;
-                to_f16(qg, a0, a2);
-                to_f16(q8, a1, a3);
-                uint2 bv = make_uint2(0u, 0u);
-                if (have) bv = *(const uint2*)(bcol + 2 * (e0 + 32 * s + 16 * half + 4 * c));
-                mma16816(dd, a0, a1, a2, a3, bv.x, bv.y);
+            for (int h = 0; h < 2; ++h) {
+                w[h][0] = lds32(b[h] + 16 + 32 * i + 4 * c);
+                w[h][1] = lds32(b[h] + 16 + 32 * i + 16 + 4 * c);
             }
-            const int gsum = (e0 + 32 * s) >> 4;
-            const float xs = sums[gsum] + sums[gsum + 1];
-            acc[0] = fmaf(off[0][s], xs, fmaf(s0[0][s], dd[0] + dd[1], acc[0]));
-            acc[1] = fmaf(off[1][s], xs, fmaf(s0[1][s], dd[2] + dd[3], acc[1]));
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {   // sub-block j = 2i + s, elements 64i + 32s ..
+                const int j = 2 * i + s;
+                float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const uint32_t qg = s ? (w[0][half] >> 4) & 0x0F0F0F0Fu : w[0][half] & 0x0F0F0F0Fu;
+                    const uint32_t q8 = s ? (w[1][half] >> 4) & 0x0F0F0F0Fu : w[1][half] & 0x0F0F0F0Fu;
+                    uint32_t a0, a2, a1, a3;
+                    to_f16(qg, a0, a2);
+                    to_f16(q8, a1, a3);
+                    uint2 bv = make_uint2(0u, 0u);
+                    if (have) bv = *(const uint2*)(bx + 2 * (64 * i + 32 * s + 16 * half));
+                    mma16816(dd, a0, a1, a2, a3, bv.x, bv.y);
+                }
+                const float xs = sx[4 * i + 2 * s] + sx[4 * i + 2 * s + 1];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    int sc, mn;
+                    if (j < 4) {
+                        sc = (W[h][0] >> (8 * j)) & 63;
+                        mn = (W[h][1] >> (8 * j)) & 63;
+                    } else {
+                        const uint32_t b8 = (W[h][2] >> (8 * (j - 4))) & 0xFF;   // byte j + 4
+                        sc = (b8 & 15) | (((W[h][0] >> (8 * (j - 4) + 6)) & 3) << 4);
+                        mn = (b8 >> 4) | (((W[h][1] >> (8 * (j - 4) + 6)) & 3) << 4);
+                    }
+                    const float s0 = sb_mul(d[h], (float)sc) * 16777216.0f;   // 2^24 undoes the subnormal encoding
+                    const float off = -sb_mul(dmin[h], (float)mn);
+                    acc[h] = fmaf(off, xs, fmaf(s0, dd[2 * h] + dd[2 * h + 1], acc[h]));
+                }
+            }
         }
     }
 };
 
 template <>
 struct KQ<SB_Q6_K> {
-    // unit u: super-block u / 4, 128-weight half hh = (u / 2) % 2, 16-weight
-    // column half H = u % 2: quadrants p = 0..3 (weights 128hh + 32p + 16H + l),
-    // one scale group each
-    __device__ static void unit(const uint8_t* tile, int rs, int u, int g, int c, const uint8_t* bcol, bool have,
-                                const float* sums, float (&acc)[2]) {
-        const int sbk = u >> 2, hh = (u >> 1) & 1, H = u & 1;
-        uint32_t q[2][4];
-        float ds[2][4];
+    // k-unit (hh, H): 128-weight half hh, 16-weight column half H; quadrants
+    // p = 0..3 are weights 128hh + 32p + 16H + l, one scale group each
+    __device__ static void superblock(const uint8_t* tile, int rs, int sbk, int g, int c, const uint8_t* bcol,
+                                      bool have, const float* sums, float (&acc)[2]) {
+        const uint8_t* b[2] = {tile + (size_t)g * rs + sbk * 210, tile + (size_t)(g + 8) * rs + sbk * 210};
+        float d[2];
+        uint32_t SW[2][4];   // the 16 int8 scales
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const uint8_t* b = tile + (size_t)(g + 8 * h) * rs + sbk * 210;
-            const uint32_t qa = lds16x2(b + 64 * hh + 16 * H + 4 * c);
-            const uint32_t qb = lds16x2(b + 64 * hh + 32 + 16 * H + 4 * c);
-            const uint32_t qh = lds16x2(b + 128 + 32 * hh + 16 * H + 4 * c);
-            q[h][0] = (qa & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
-            q[h][1] = (qb & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
-            q[h][2] = ((qa >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
-            q[h][3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
-            const float d = __half2float(__ushort_as_half(*(const unsigned short*)(b + 208)));
-            const int8_t* sc = (const int8_t*)(b + 192 + 8 * hh + H);
+            d[h] = __half2float(__ushort_as_half(*(const unsigned short*)(b[h] + 208)));
 #pragma unroll
-            for (int pq = 0; pq < 4; ++pq) ds[h][pq] = sb_mul(d, (float)sc[2 * pq]);
+            for (int q = 0; q < 4; ++q) SW[h][q] = lds16x2(b[h] + 192 + 4 * q);
         }
+        const uint8_t* bx = bcol + 2 * (sbk * 256 + 4 * c);
+        const float* sx = sums + sbk * 16;
 #pragma unroll
-        for (int pq = 0; pq < 4; ++pq) {
-            const int e = sbk * 256 + 128 * hh + 32 * pq + 16 * H;   // first element of the group
-            uint32_t a0, a2, a1, a3;
-            to_f16(q[0][pq], a0, a2);
-            to_f16(q[1][pq], a1, a3);
-            uint2 bv = make_uint2(0u, 0u);
-            if (have) bv = *(const uint2*)(bcol + 2 * (e + 4 * c));
-            float dd[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(dd, a0, a1, a2, a3, bv.x, bv.y);
-            const float xs = 32.f * sums[e >> 4];
-            acc[0] = fmaf(ds[0][pq], fmaf(dd[0] + dd[1], 16777216.0f, -xs), acc[0]);
-            acc[1] = fmaf(ds[1][pq], fmaf(dd[2] + dd[3], 16777216.0f, -xs), acc[1]);
+        for (int u = 0; u < 4; ++u) {
+            const int hh = u >> 1, H = u & 1;
+            uint32_t q[2][4];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t qa = lds16x2(b[h] + 64 * hh + 16 * H + 4 * c);
+                const uint32_t qb = lds16x2(b[h] + 64 * hh + 32 + 16 * H + 4 * c);
+                const uint32_t qh = lds16x2(b[h] + 128 + 32 * hh + 16 * H + 4 * c);
+                q[h][0] = (qa & 0x0F0F0F0Fu) | ((qh << 4) & 0x30303030u);
+                q[h][1] = (qb & 0x0F0F0F0Fu) | ((qh << 2) & 0x30303030u);
+                q[h][2] = ((qa >> 4) & 0x0F0F0F0Fu) | (qh & 0x30303030u);
+                q[h][3] = ((qb >> 4) & 0x0F0F0F0Fu) | ((qh >> 2) & 0x30303030u);
+            }
+#pragma unroll
+            for (int pq = 0; pq < 4; ++pq) {
+                const int e = 128 * hh + 32 * pq + 16 * H;   // group's first element in the super-block
+                uint32_t a0, a2, a1, a3;
+                to_f16(q[0][pq], a0, a2);
+                to_f16(q[1][pq], a1, a3);
+                uint2 bv = make_uint2(0u, 0u);
+                if (have) bv = *(const uint2*)(bx + 2 * e);
+                float dd[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(dd, a0, a1, a2, a3, bv.x, bv.y);
+                const float xs = 32.f * sx[e >> 4];
+                const int idx = 8 * hh + 2 * pq + H;   // the group's scale: a constant after unrolling
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const float sc = (float)(int8_t)((SW[h][idx >> 2] >> (8 * (idx & 3))) & 0xFF);
+                    acc[h] = fmaf(sb_mul(d[h], sc), fmaf(dd[2 * h] + dd[2 * h + 1], 16777216.0f, -xs), acc[h]);
+                }
+            }
         }
     }
 };
@@ -415,13 +433,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
         descs[threadIdx.x].seq = -1;
     }
     __syncthreads();
+    // programmatic dependent launch: the next kernel on the stream may start its
+    // prologue (plan, weight copies) as SMs free up. Everything this kernel
+    // reads that an earlier kernel of the block writes (x, h, v), and every
+    // global write, comes after griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;");
     if (warp == kW) {
         build_plan(p, smem);
-    } else if (GU) {
-        // the tokens' x, rows 0..T-1
-        stage_rows(smem, kMaxTok, p.k, [&](int r) { return r < p.n_tokens ? p.x + (size_t)r * p.d_model : nullptr; });
+        plan_arrive();
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (GU)   // the tokens' x, rows 0..T-1
+            stage_rows(smem, kMaxTok, p.k, [&](int r) { return r < p.n_tokens ? p.x + (size_t)r * p.d_model : nullptr; });
+        plan_wait();
     }
-    __syncthreads();
 
     const int nd = ((const int*)(smem + Smem::misc))[0];
     const int R = p.rows_out / (GU ? 8 : 16);   // items per distinct expert
@@ -490,9 +515,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
 
     // -------------------------------------------------------------- consumers
     const int g = lane >> 2, c = lane & 3;
-    const int units = p.k / 64;
-    const int wpt = units % kMaxWpt == 0 ? kMaxWpt : units % 4 == 0 ? 4 : units % 2 == 0 ? 2 : 1;   // P >= 2 items at once
-    const int upw = units / wpt, P = kW / wpt, pos = warp / wpt, wsub = warp % wpt;
+    // one super-block per warp: k / 256 warps per item (<= 8), P items at once
+    const int wpt = p.k / 256;
+    const int P = kW / wpt, pos = warp / wpt, wsub = warp % wpt;
     const int* s_dist = (const int*)(smem + Smem::p_dist);
     const int* s_mask = (const int*)(smem + Smem::p_mask);
     const int* s_first = (const int*)(smem + Smem::p_first);
@@ -520,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
             });
         }
         first_chunk = false;
-        for (int m = pos; m < ce - cs; m += P) {
+        for (int m = pos; pos < P && m < ce - cs; m += P) {
             const int sq = seq + m;
             const int s = sq % kStages;
             const bool stamped = wait_seq(&descs[s].seq, sq, p.err, abort_flag);
@@ -536,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
             float acc[2] = {0.f, 0.f};
             if (!bad) {
                 const uint8_t* tile = smem + Smem::stages + s * kStageBytes;
-                for (int u = wsub * upw; u < (wsub + 1) * upw; ++u) KQ<QT>::unit(tile, p.rs, u, g, c, bcol, have, csum, acc);
+                KQ<QT>::superblock(tile, p.rs, wsub, g, c, bcol, have, csum, acc);
             }
             red[(s * kMaxWpt + wsub) * 32 + lane] = make_float2(acc[0], acc[1]);
             __threadfence_block();
@@ -603,6 +628,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
 // weights (NaN for bad ids) are read once per CTA into shared memory.
 __global__ void k_small_combine(const SmallParams p, const float* w, float* out, int accumulate) {
     __shared__ float s_w[kMaxPairs];
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int n_pairs = p.n_tokens * p.n_used;
     for (int q = threadIdx.x; q < n_pairs; q += blockDim.x) {
         const int t = q / p.n_used, e = q % p.n_used;
@@ -668,6 +695,22 @@ bool small_enabled() {
 // row-by-row copies)
 int staged_stride(int rb) { return (pad_enabled() && rb % 16 == 0 && (rb / 16) % 2 == 0) ? rb + 16 : rb; }
 
+// launched with programmatic stream serialization (see the kernel)
+template <class K, class... Args>
+bool launch_pdl(K kernel, int grid, int threads, int smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return sb_cuda_ok(cudaLaunchKernelEx(&cfg, kernel, args...), "small-batch launch");
+}
+
 template <int QT, bool GU>
 bool launch_small(const SmallParams& p, cudaStream_t st, int slot) {
     if (!g_attr[slot]) {
@@ -676,8 +719,7 @@ bool launch_small(const SmallParams& p, cudaStream_t st, int slot) {
             return false;
         g_attr[slot] = true;
     }
-    k_small<QT, GU><<<g_sms, kThreads, Smem::total, st>>>(p);
-    return true;
+    return launch_pdl(k_small<QT, GU>, g_sms, kThreads, Smem::total, st, p);
 }
 
 bool kq_type(int qt) { return qt == SB_Q4_K || qt == SB_Q6_K; }
@@ -752,7 +794,8 @@ int sb_try_block_small(const sb_block_args& a, cudaStream_t st) {
     if (!ok2) return -1;
     const int t3 = sb_timing_begin("small_kq_combine", st);
     const long long n = (long long)a.n_tokens * a.d_model;
-    k_small_combine<<<(int)std::min<long long>((n + 255) / 256, 4LL * g_sms), 256, 0, st>>>(pd, a.w, a.out, a.accumulate);
+    const bool ok3 = launch_pdl(k_small_combine, (int)std::min<long long>((n + 255) / 256, 4LL * g_sms), 256, 0, st, pd,
+                                a.w, a.out, a.accumulate);
     sb_timing_end(t3, st);
-    return sb_cuda_ok(cudaGetLastError(), "small-batch block launch") ? 1 : -1;
+    return ok3 ? 1 : -1;
 }

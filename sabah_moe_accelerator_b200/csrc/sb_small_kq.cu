@@ -71,16 +71,15 @@ struct Desc {
 struct Smem {
     static constexpr int stages = 0;
     static constexpr int barea = stages + kStages * kStageBytes;
-    static constexpr int sums = barea + kBArea;                         // [rows][k / 16] float
-    static constexpr int red = sums + kMaxGroups * 4;                   // [kStages][kMaxWpt][32] float2
+    static constexpr int sums = barea + kBArea;                         // [rows][k / 16] float: sum of x
+    static constexpr int inv = sums + kMaxGroups * 4;                   // [rows][k / 16] float: 2^-scale
+    static constexpr int red = inv + kMaxGroups * 4;                    // [kStages][kMaxWpt][32] float2
     static constexpr int p_e = red + kStages * kMaxWpt * 32 * 8;        // [kMaxPairs] pair -> expert id (-1 bad)
     static constexpr int p_dist = p_e + kMaxPairs * 4;                  // [kMaxPairs] pair -> distinct index
     static constexpr int p_expert = p_dist + kMaxPairs * 4;             // [kMaxPairs] distinct -> expert id
     static constexpr int p_mask = p_expert + kMaxPairs * 4;             // [kMaxPairs] distinct -> token mask
     static constexpr int p_first = p_mask + kMaxPairs * 4;              // [kMaxPairs][kMaxTok] first pair
-    static constexpr int rowmax = p_first + kMaxPairs * kMaxTok * 4;    // [8] staged-row max (float bits)
-    static constexpr int rowexp = rowmax + 32;                          // [8] staged-row exponent
-    static constexpr int misc = rowexp + 32;                            // n_distinct, abort
+    static constexpr int misc = p_first + kMaxPairs * kMaxTok * 4;      // n_distinct, abort
     static constexpr int desc = misc + 16;                              // [kStages] Desc
     static constexpr int cnt = desc + kStages * (int)sizeof(Desc);      // [kStages] int
     static constexpr int bars = (cnt + kStages * 4 + 7) & ~7;           // full[kStages], empty[kStages]
@@ -213,74 +212,49 @@ __device__ void build_plan(const SmallParams& p, uint8_t* smem) {
 
 // ------------------------------------------------------------ B staging
 // n_rows rows of k fp32 values (row r from src(r), nullptr = zeros) into the B
-// area as fp16 hi + lo, each row scaled by 2^rowexp[r] (its max into
-// [2^13, 2^14)), and the scaled sums of every 16 elements. Consumer threads
-// only; n_rows * k / 16 <= kMaxGroups. Ends with consumers_sync.
+// area as fp16 hi + lo. Each 16-element group is scaled by its own power of
+// two (max into [2^13, 2^14)), whose inverse goes to inv[], and its plain sum
+// to sums[]. One group per consumer thread, one pass; ends with
+// consumers_sync. n_rows * k / 16 <= kMaxGroups.
 template <class Src>
 __device__ void stage_rows(uint8_t* smem, int n_rows, int k, Src src) {
-    const int tid = threadIdx.x;
+    const int gi = threadIdx.x;
     const int gpr = k / 16, ng = n_rows * gpr;
-    int* rowmax = (int*)(smem + Smem::rowmax);
-    int* rowexp = (int*)(smem + Smem::rowexp);
-    float* sums = (float*)(smem + Smem::sums);
-    if (tid < 8) rowmax[tid] = 0;
-    consumers_sync();
-    float4 v[2][4];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int gi = tid + kCThreads * u;
-        const float* s = gi < ng ? src(gi / gpr) : nullptr;
-        float m = 0.f;
+    if (gi < ng) {
+        const int row = gi / gpr, g16 = gi % gpr;
+        const float* s = src(row);
+        float4 v[4];
+        float m = 0.f, sum = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            v[u][j] = s ? __ldcg((const float4*)(s + 16 * (gi % gpr)) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-            m = fmaxf(m, fmaxf(fmaxf(fabsf(v[u][j].x), fabsf(v[u][j].y)), fmaxf(fabsf(v[u][j].z), fabsf(v[u][j].w))));
+            v[j] = s ? __ldcg((const float4*)(s + 16 * g16) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+            sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
         }
-        // non-negative floats order like their bit patterns (a NaN input is
-        // ignored by fmaxf here and reaches the output through the MMA)
-        if (s && m > 0.f) atomicMax(rowmax + gi / gpr, __float_as_int(m));
-    }
-    consumers_sync();
-    const int stride = 2 * k + 32;
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int gi = tid + kCThreads * u;
-        if (gi >= ng) continue;
-        const int row = gi / gpr, g16 = gi % gpr;
-        const float m = __int_as_float(rowmax[row]);
         int ex = 0;
         if (m > 0.f && isfinite(m)) {
-            frexpf(m, &ex);
+            frexpf(m, &ex);   // m = f * 2^ex, f in [0.5, 1)
             ex = max(-100, min(100, 14 - ex));
         }
-        if (g16 == 0) rowexp[row] = ex;
         const float sc = ldexpf(1.f, ex);
-        float f[16];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            f[4 * j] = v[u][j].x * sc;
-            f[4 * j + 1] = v[u][j].y * sc;
-            f[4 * j + 2] = v[u][j].z * sc;
-            f[4 * j + 3] = v[u][j].w * sc;
-        }
-        float sum = 0.f;
         uint32_t hw[8], lw[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const float a = f[2 * j], b = f[2 * j + 1];
-            sum += a + b;
+            const float4 q = v[j >> 1];
+            const float a = ((j & 1) ? q.z : q.x) * sc, b = ((j & 1) ? q.w : q.y) * sc;
             const float ah = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
             const float bh = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
             const __half2 hh = __floats2half2_rn(ah, bh), ll = __floats2half2_rn(a - ah, b - bh);
             hw[j] = *(const uint32_t*)&hh;
             lw[j] = *(const uint32_t*)&ll;
         }
-        uint8_t* hrow = smem + Smem::barea + row * stride + 32 * g16;
+        uint8_t* hrow = smem + Smem::barea + row * (2 * k + 32) + 32 * g16;
         *(uint4*)hrow = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         *(uint4*)(hrow + 16) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
         *(uint4*)(hrow + kLoOff) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         *(uint4*)(hrow + kLoOff + 16) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-        sums[row * gpr + g16] = sum;
+        ((float*)(smem + Smem::sums))[gi] = sum;
+        ((float*)(smem + Smem::inv))[gi] = ldexpf(1.f, -ex);
     }
     consumers_sync();
 }
@@ -299,14 +273,14 @@ struct KQ<SB_Q4_K> {
     // k-unit i: quant bytes 32i .. 32i + 31; low nibbles are sub-block 2i,
     // high nibbles sub-block 2i + 1
     __device__ static void superblock(const uint8_t* tile, int rs, int sbk, int g, int c, const uint8_t* bcol,
-                                      bool have, const float* sums, float (&acc)[2]) {
+                                      bool have, const float* sums, const float* inv, float (&acc)[2]) {
         const uint8_t* b[2] = {tile + (size_t)g * rs + sbk * 144, tile + (size_t)(g + 8) * rs + sbk * 144};
         float d[2], dmin[2];
         uint32_t W[2][3];   // the 12 scale bytes (ggml's get_scale_min_k4 packing, as sb_kscale)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const uint32_t dm = lds32(b[h]);
-            d[h] = __half2float(__ushort_as_half((unsigned short)(dm & 0xFFFF)));
+            d[h] = __half2float(__ushort_as_half((unsigned short)(dm & 0xFFFF))) * 16777216.0f;   // 2^24: subnormal A
             dmin[h] = __half2float(__ushort_as_half((unsigned short)(dm >> 16)));
             W[h][0] = lds32(b[h] + 4);
             W[h][1] = lds32(b[h] + 8);
@@ -314,6 +288,7 @@ struct KQ<SB_Q4_K> {
         }
         const uint8_t* bx = bcol + 2 * (sbk * 256 + 4 * c);
         const float* sx = sums + sbk * 16;
+        const float* ix = inv + sbk * 16;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint32_t w[2][2];
@@ -325,7 +300,7 @@ struct KQ<SB_Q4_K> {
 #pragma unroll
             for (int s = 0; s < 2; ++s) {   // sub-block j = 2i + s, elements 64i + 32s ..
                 const int j = 2 * i + s;
-                float dd[4] = {0.f, 0.f, 0.f, 0.f};
+                float dd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};   // per 16-element half
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     const uint32_t qg = s ? (w[0][half] >> 4) & 0x0F0F0F0Fu : w[0][half] & 0x0F0F0F0Fu;
@@ -335,9 +310,10 @@ struct KQ<SB_Q4_K> {
                     to_f16(q8, a1, a3);
                     uint2 bv = make_uint2(0u, 0u);
                     if (have) bv = *(const uint2*)(bx + 2 * (64 * i + 32 * s + 16 * half));
-                    mma16816(dd, a0, a1, a2, a3, bv.x, bv.y);
+                    mma16816(dd[half], a0, a1, a2, a3, bv.x, bv.y);
                 }
-                const float xs = sx[4 * i + 2 * s] + sx[4 * i + 2 * s + 1];
+                const int gq = 4 * i + 2 * s;   // the sub-block's two 16-element groups
+                const float xs = sx[gq] + sx[gq + 1], i0 = ix[gq], i1 = ix[gq + 1];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     int sc, mn;
@@ -349,9 +325,10 @@ struct KQ<SB_Q4_K> {
                         sc = (b8 & 15) | (((W[h][0] >> (8 * (j - 4) + 6)) & 3) << 4);
                         mn = (b8 >> 4) | (((W[h][1] >> (8 * (j - 4) + 6)) & 3) << 4);
                     }
-                    const float s0 = sb_mul(d[h], (float)sc) * 16777216.0f;   // 2^24 undoes the subnormal encoding
+                    const float s0 = sb_mul(d[h], (float)sc);
                     const float off = -sb_mul(dmin[h], (float)mn);
-                    acc[h] = fmaf(off, xs, fmaf(s0, dd[2 * h] + dd[2 * h + 1], acc[h]));
+                    const float dot = fmaf(dd[0][2 * h] + dd[0][2 * h + 1], i0, (dd[1][2 * h] + dd[1][2 * h + 1]) * i1);
+                    acc[h] = fmaf(off, xs, fmaf(s0, dot, acc[h]));
                 }
             }
         }
@@ -363,7 +340,7 @@ struct KQ<SB_Q6_K> {
     // k-unit (hh, H): 128-weight half hh, 16-weight column half H; quadrants
     // p = 0..3 are weights 128hh + 32p + 16H + l, one scale group each
     __device__ static void superblock(const uint8_t* tile, int rs, int sbk, int g, int c, const uint8_t* bcol,
-                                      bool have, const float* sums, float (&acc)[2]) {
+                                      bool have, const float* sums, const float* inv, float (&acc)[2]) {
         const uint8_t* b[2] = {tile + (size_t)g * rs + sbk * 210, tile + (size_t)(g + 8) * rs + sbk * 210};
         float d[2];
         uint32_t SW[2][4];   // the 16 int8 scales
@@ -375,6 +352,7 @@ struct KQ<SB_Q6_K> {
         }
         const uint8_t* bx = bcol + 2 * (sbk * 256 + 4 * c);
         const float* sx = sums + sbk * 16;
+        const float* ix = inv + sbk * 16;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int hh = u >> 1, H = u & 1;
@@ -399,12 +377,12 @@ struct KQ<SB_Q6_K> {
                 if (have) bv = *(const uint2*)(bx + 2 * e);
                 float dd[4] = {0.f, 0.f, 0.f, 0.f};
                 mma16816(dd, a0, a1, a2, a3, bv.x, bv.y);
-                const float xs = 32.f * sx[e >> 4];
+                const float xs = 32.f * sx[e >> 4], iv = ix[e >> 4] * 16777216.0f;   // 2^24: subnormal A
                 const int idx = 8 * hh + 2 * pq + H;   // the group's scale: a constant after unrolling
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const float sc = (float)(int8_t)((SW[h][idx >> 2] >> (8 * (idx & 3))) & 0xFF);
-                    acc[h] = fmaf(sb_mul(d[h], sc), fmaf(dd[2 * h] + dd[2 * h + 1], 16777216.0f, -xs), acc[h]);
+                    acc[h] = fmaf(sb_mul(d[h], sc), fmaf(dd[2 * h] + dd[2 * h + 1], iv, -xs), acc[h]);
                 }
             }
         }
@@ -521,8 +499,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
     const int* s_dist = (const int*)(smem + Smem::p_dist);
     const int* s_mask = (const int*)(smem + Smem::p_mask);
     const int* s_first = (const int*)(smem + Smem::p_first);
-    const int* rowexp = (const int*)(smem + Smem::rowexp);
     const float* sums = (const float*)(smem + Smem::sums);
+    const float* invs = (const float*)(smem + Smem::inv);
     float2* red = (float2*)(smem + Smem::red);
     int* cnt = (int*)(smem + Smem::cnt);
     const int n_pairs = p.n_tokens * p.n_used;
@@ -557,11 +535,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
             const int brow = GU ? (g >> 1) : 4 * (dd - d0) + (g >> 1);
             const bool have = GU ? (g >> 1) < p.n_tokens : (g >> 1) < __popc((unsigned)s_mask[dd]);
             const uint8_t* bcol = smem + Smem::barea + brow * stride + ((g & 1) ? kLoOff : 0);
-            const float* csum = sums + (GU ? c : 4 * (dd - d0) + c) * gpr;
+            const int crow = (GU ? c : 4 * (dd - d0) + c) * gpr;   // column c's staged row
             float acc[2] = {0.f, 0.f};
             if (!bad) {
                 const uint8_t* tile = smem + Smem::stages + s * kStageBytes;
-                KQ<QT>::superblock(tile, p.rs, wsub, g, c, bcol, have, csum, acc);
+                KQ<QT>::superblock(tile, p.rs, wsub, g, c, bcol, have, sums + crow, invs + crow, acc);
             }
             red[(s * kMaxWpt + wsub) * 32 + lane] = make_float2(acc[0], acc[1]);
             __threadfence_block();
@@ -594,8 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
             const unsigned mask = (unsigned)s_mask[dd];
             if (GU) {
                 // column c is token c: rows g (gate) and g + 8 (up) of 8-row block r
-                const float sc = c < p.n_tokens ? ldexpf(1.f, -rowexp[c]) : 0.f;
-                const float gv = v0 * sc, uv = v1 * sc;
+                const float gv = v0, uv = v1;
                 const float hv = gv / (1.f + expf(-gv)) * uv;
                 for (int half = 0; half < 2; ++half)
                     for (unsigned mm = half ? m1 : m0; mm; mm &= mm - 1) {
@@ -606,14 +583,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
                 // column c is the expert's c-th token: rows g and g + 8 of 16-row tile r
                 if (c < __popc(mask)) {
                     const int t = nth_bit(mask, c);
-                    const float sc = ldexpf(1.f, -rowexp[4 * (dd - d0) + c]);
                     for (int half = 0; half < 2; ++half)
                         for (unsigned mm = half ? m1 : m0; mm; mm &= mm - 1) {
                             const int pr = __ffs(mm) - 1 + 32 * half;
                             if (pr / p.n_used == t) {
                                 float* o = p.v + (size_t)pr * p.d_model + 16 * r;
-                                o[g] = v0 * sc;
-                                o[g + 8] = v1 * sc;
+                                o[g] = v0;
+                                o[g + 8] = v1;
                             }
                         }
                 }

@@ -475,9 +475,25 @@ def run_ep(args, rank: int, world: int, local_rank: int):
         if world > 1:
             dist.barrier()
 
+    # warm every routing set (the runtime sizes its scratch), then one CUDA graph
+    # per set: the 48 blocks' kernels and NCCL collectives replay without host work
+    with torch.cuda.stream(stream):
+        for s in range(EP_SETS):
+            step(s)
+    stream.synchronize()
+    barrier()
+    graphs = []
+    with torch.cuda.stream(stream):
+        for s in range(EP_SETS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(s)
+            graphs.append(g)
+    stream.synchronize()
+    barrier()
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
-            step(i % EP_SETS)
+            graphs[i % EP_SETS].replay()
     stream.synchronize()
     clocks = ClockSampler(local_rank)
     barrier()
@@ -487,7 +503,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
     with torch.cuda.stream(stream):
         t_0.record(stream)
         for i in range(args.steps):
-            step(i % EP_SETS)
+            graphs[i % EP_SETS].replay()
         t_1.record(stream)
     stream.synchronize()
     torch.cuda.synchronize()
@@ -498,6 +514,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
+    del graphs   # graphs holding NCCL calls go before the process group does
 
     # per-kernel device times over one step (eager, events on the launching stream)
     L.sabah_rt_kernel_timing(1)
@@ -571,7 +588,8 @@ def run_ep(args, rank: int, world: int, local_rank: int):
                    "experts_per_gpu": n_loc, "routing_sets": EP_SETS,
                    "l2": "inputs larger than L2: ~%.1f GB of distinct expert bytes per step over all GPUs"
                          % (totals[0].item() / 1e9),
-                   "parallelism": "ep%d" % world, "exchange": "NCCL all-gather + reduce-scatter per block"},
+                   "parallelism": "ep%d" % world, "exchange": "NCCL all-gather + reduce-scatter per block",
+                   "replay": "one CUDA graph per routing set (kernels and collectives)"},
         "roofline": roofline,
         "e2e": {"value": round(EP_TOKENS * 1e3 / e_ms, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x_h.numel() * 4 + h2d[0] / e_steps),

@@ -2,8 +2,9 @@
 // experts live on this GPU are gathered out of the all-gathered activations,
 // pushed through the fused block as one "token" each, and their weighted
 // outputs are summed back into token rows in a fixed order before the
-// reduce-scatter. All three are plain HBM-bound copies / sums of fp32 rows,
-// vectorised as float4 with one warp per row and a grid of 4 CTAs per SM.
+// reduce-scatter. All three are plain copies / sums of a few hundred KB of
+// fp32 rows: one thread per float4 of the output, so every load of a launch is
+// in flight at once (the work is latency-bound, not bandwidth-bound).
 #include <algorithm>
 
 #include "sb_kernels.h"
@@ -24,44 +25,48 @@ int sm_count() {
     }
     return sms;
 }
-// warps = rows, 8 per CTA; at most 4 CTAs per SM
-int grid_rows(long long rows) { return (int)std::max(1LL, std::min((rows + 7) / 8, 4LL * sm_count())); }
-int grid_elems(long long n4) { return (int)std::max(1LL, std::min((n4 + kThreads - 1) / kThreads, 4LL * sm_count())); }
+// one thread per float4 of the output, at most 8 CTAs per SM
+int grid_elems(long long n4) { return (int)std::max(1LL, std::min((n4 + kThreads - 1) / kThreads, 8LL * sm_count())); }
 
 // dst[i] = src[rows[i]]; a row index outside [0, n_src) gives a zero row
 __global__ void k_gather_rows(const float4* src, int n_src, const int32_t* rows, int n, int k4, float4* dst) {
-    const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int nw = gridDim.x * (kThreads / 32);
-    for (int i = warp; i < n; i += nw) {
-        const int r = rows[i];
-        float4* d = dst + (size_t)i * k4;
-        if (r < 0 || r >= n_src) {
-            for (int j = lane; j < k4; j += 32) d[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-            continue;
-        }
-        const float4* s = src + (size_t)r * k4;
-        for (int j = lane; j < k4; j += 32) d[j] = __ldg(s + j);
+    const long long total = (long long)n * k4;
+    for (long long q = blockIdx.x * (long long)kThreads + threadIdx.x; q < total; q += (long long)gridDim.x * kThreads) {
+        const int i = (int)(q / k4), j = (int)(q % k4);
+        const int r = __ldg(rows + i);
+        dst[q] = (r < 0 || r >= n_src) ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(src + (size_t)r * k4 + j);
     }
 }
 
 // dst[t] = sum_{i in [off[t], off[t+1])} src[i], in increasing i (offsets
-// clamped to [0, n_src])
+// clamped to [0, n_src]); the rows' loads are issued before the adds
 __global__ void k_sum_rows(const float4* src, int n_src, const int32_t* off, int n_out, int k4, float4* dst) {
-    const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int nw = gridDim.x * (kThreads / 32);
-    for (int t = warp; t < n_out; t += nw) {
-        const int i0 = max(off[t], 0), i1 = min(off[t + 1], n_src);
-        for (int j = lane; j < k4; j += 32) {
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int i = i0; i < i1; ++i) {
-                const float4 v = __ldg(src + (size_t)i * k4 + j);
-                a.x += v.x;
-                a.y += v.y;
-                a.z += v.z;
-                a.w += v.w;
+    const long long total = (long long)n_out * k4;
+    for (long long q = blockIdx.x * (long long)kThreads + threadIdx.x; q < total; q += (long long)gridDim.x * kThreads) {
+        const int t = (int)(q / k4), j = (int)(q % k4);
+        const int i0 = max(__ldg(off + t), 0), i1 = min(__ldg(off + t + 1), n_src);
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        int i = i0;
+        for (; i + 4 <= i1; i += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldg(src + (size_t)(i + u) * k4 + j);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                a.x += v[u].x;
+                a.y += v[u].y;
+                a.z += v[u].z;
+                a.w += v[u].w;
             }
-            dst[(size_t)t * k4 + j] = a;
         }
+        for (; i < i1; ++i) {
+            const float4 v = __ldg(src + (size_t)i * k4 + j);
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
+        }
+        dst[q] = a;
     }
 }
 
@@ -86,8 +91,8 @@ SABAH_API int sabah_ep_gather_rows(const float* d_src, int n_src, const int32_t*
     }
     if (n == 0) return 0;
     const int tslot = sb_timing_begin("ep_gather_rows", (cudaStream_t)stream);
-    k_gather_rows<<<grid_rows(n), kThreads, 0, (cudaStream_t)stream>>>((const float4*)d_src, n_src, d_rows, n,
-                                                                       k / 4, (float4*)d_dst);
+    k_gather_rows<<<grid_elems((long long)n * (k / 4)), kThreads, 0, (cudaStream_t)stream>>>(
+        (const float4*)d_src, n_src, d_rows, n, k / 4, (float4*)d_dst);
     sb_timing_end(tslot, (cudaStream_t)stream);
     return sb_cuda_ok(cudaGetLastError(), "ep gather launch") ? 0 : -1;
 }
@@ -101,8 +106,8 @@ SABAH_API int sabah_ep_sum_rows(const float* d_src, int n_src, const int32_t* d_
     }
     if (n_out == 0) return 0;
     const int tslot = sb_timing_begin("ep_sum_rows", (cudaStream_t)stream);
-    k_sum_rows<<<grid_rows(n_out), kThreads, 0, (cudaStream_t)stream>>>((const float4*)d_src, n_src, d_offsets, n_out,
-                                                                        k / 4, (float4*)d_dst);
+    k_sum_rows<<<grid_elems((long long)n_out * (k / 4)), kThreads, 0, (cudaStream_t)stream>>>(
+        (const float4*)d_src, n_src, d_offsets, n_out, k / 4, (float4*)d_dst);
     sb_timing_end(tslot, (cudaStream_t)stream);
     return sb_cuda_ok(cudaGetLastError(), "ep sum launch") ? 0 : -1;
 }

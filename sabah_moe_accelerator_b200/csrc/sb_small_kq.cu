@@ -110,10 +110,27 @@ __device__ inline void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(k
 __device__ inline void plan_arrive() { asm volatile("bar.arrive 2, %0;" ::"n"(kThreads) : "memory"); }
 __device__ inline void plan_wait() { asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory"); }
 
-__device__ inline uint32_t lds32(const uint8_t* p) { return *(const uint32_t*)p; }
-__device__ inline uint32_t lds16x2(const uint8_t* p) {   // 4 bytes at a 2-byte-aligned address
-    return (uint32_t) * (const unsigned short*)p | ((uint32_t) * (const unsigned short*)(p + 2) << 16);
+// shared-memory loads at 32-bit shared addresses (explicit state space: a
+// generic load would wait on the long scoreboard)
+__device__ inline uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
 }
+__device__ inline uint32_t lds16(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ inline uint32_t lds16x2(uint32_t a) {   // 4 bytes at a 2-byte-aligned address
+    return lds16(a) | (lds16(a + 2) << 16);
+}
+__device__ inline uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ inline float ldsf(uint32_t a) { return __uint_as_float(lds32(a)); }
 // the j-th set bit (from bit 0) of a token mask
 __device__ inline int nth_bit(unsigned m, int j) {
     for (int b = 0; b < kMaxTok; ++b)
@@ -272,9 +289,9 @@ template <>
 struct KQ<SB_Q4_K> {
     // k-unit i: quant bytes 32i .. 32i + 31; low nibbles are sub-block 2i,
     // high nibbles sub-block 2i + 1
-    __device__ static void superblock(const uint8_t* tile, int rs, int sbk, int g, int c, const uint8_t* bcol,
-                                      bool have, const float* sums, const float* inv, float (&acc)[2]) {
-        const uint8_t* b[2] = {tile + (size_t)g * rs + sbk * 144, tile + (size_t)(g + 8) * rs + sbk * 144};
+    __device__ static void superblock(uint32_t tile, int rs, int sbk, int g, int c, uint32_t bcol, bool have,
+                                      uint32_t sums, uint32_t inv, float (&acc)[2]) {
+        const uint32_t b[2] = {tile + (uint32_t)(g * rs + sbk * 144), tile + (uint32_t)((g + 8) * rs + sbk * 144)};
         float d[2], dmin[2];
         uint32_t W[2][3];   // the 12 scale bytes (ggml's get_scale_min_k4 packing, as sb_kscale)
 #pragma unroll
@@ -286,9 +303,8 @@ struct KQ<SB_Q4_K> {
             W[h][1] = lds32(b[h] + 8);
             W[h][2] = lds32(b[h] + 12);
         }
-        const uint8_t* bx = bcol + 2 * (sbk * 256 + 4 * c);
-        const float* sx = sums + sbk * 16;
-        const float* ix = inv + sbk * 16;
+        const uint32_t bx = bcol + 2 * (sbk * 256 + 4 * c);
+        const uint32_t sx = sums + 4 * sbk * 16, ix = inv + 4 * sbk * 16;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             uint32_t w[2][2];
@@ -309,11 +325,11 @@ struct KQ<SB_Q4_K> {
                     to_f16(qg, a0, a2);
                     to_f16(q8, a1, a3);
                     uint2 bv = make_uint2(0u, 0u);
-                    if (have) bv = *(const uint2*)(bx + 2 * (64 * i + 32 * s + 16 * half));
+                    if (have) bv = lds64(bx + 2 * (64 * i + 32 * s + 16 * half));
                     mma16816(dd[half], a0, a1, a2, a3, bv.x, bv.y);
                 }
                 const int gq = 4 * i + 2 * s;   // the sub-block's two 16-element groups
-                const float xs = sx[gq] + sx[gq + 1], i0 = ix[gq], i1 = ix[gq + 1];
+                const float xs = ldsf(sx + 4 * gq) + ldsf(sx + 4 * gq + 4), i0 = ldsf(ix + 4 * gq), i1 = ldsf(ix + 4 * gq + 4);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     int sc, mn;
@@ -339,20 +355,19 @@ template <>
 struct KQ<SB_Q6_K> {
     // k-unit (hh, H): 128-weight half hh, 16-weight column half H; quadrants
     // p = 0..3 are weights 128hh + 32p + 16H + l, one scale group each
-    __device__ static void superblock(const uint8_t* tile, int rs, int sbk, int g, int c, const uint8_t* bcol,
-                                      bool have, const float* sums, const float* inv, float (&acc)[2]) {
-        const uint8_t* b[2] = {tile + (size_t)g * rs + sbk * 210, tile + (size_t)(g + 8) * rs + sbk * 210};
+    __device__ static void superblock(uint32_t tile, int rs, int sbk, int g, int c, uint32_t bcol, bool have,
+                                      uint32_t sums, uint32_t inv, float (&acc)[2]) {
+        const uint32_t b[2] = {tile + (uint32_t)(g * rs + sbk * 210), tile + (uint32_t)((g + 8) * rs + sbk * 210)};
         float d[2];
         uint32_t SW[2][4];   // the 16 int8 scales
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            d[h] = __half2float(__ushort_as_half(*(const unsigned short*)(b[h] + 208)));
+            d[h] = __half2float(__ushort_as_half((unsigned short)lds16(b[h] + 208)));
 #pragma unroll
             for (int q = 0; q < 4; ++q) SW[h][q] = lds16x2(b[h] + 192 + 4 * q);
         }
-        const uint8_t* bx = bcol + 2 * (sbk * 256 + 4 * c);
-        const float* sx = sums + sbk * 16;
-        const float* ix = inv + sbk * 16;
+        const uint32_t bx = bcol + 2 * (sbk * 256 + 4 * c);
+        const uint32_t sx = sums + 4 * sbk * 16, ix = inv + 4 * sbk * 16;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int hh = u >> 1, H = u & 1;
@@ -374,10 +389,10 @@ struct KQ<SB_Q6_K> {
                 to_f16(q[0][pq], a0, a2);
                 to_f16(q[1][pq], a1, a3);
                 uint2 bv = make_uint2(0u, 0u);
-                if (have) bv = *(const uint2*)(bx + 2 * e);
+                if (have) bv = lds64(bx + 2 * e);
                 float dd[4] = {0.f, 0.f, 0.f, 0.f};
                 mma16816(dd, a0, a1, a2, a3, bv.x, bv.y);
-                const float xs = 32.f * sx[e >> 4], iv = ix[e >> 4] * 16777216.0f;   // 2^24: subnormal A
+                const float xs = 32.f * ldsf(sx + 4 * (e >> 4)), iv = ldsf(ix + 4 * (e >> 4)) * 16777216.0f;   // 2^24: subnormal A
                 const int idx = 8 * hh + 2 * pq + H;   // the group's scale: a constant after unrolling
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
@@ -534,12 +549,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
             // this lane's B column g: GU token g / 2, down the expert's (g / 2)-th token; part g % 2
             const int brow = GU ? (g >> 1) : 4 * (dd - d0) + (g >> 1);
             const bool have = GU ? (g >> 1) < p.n_tokens : (g >> 1) < __popc((unsigned)s_mask[dd]);
-            const uint8_t* bcol = smem + Smem::barea + brow * stride + ((g & 1) ? kLoOff : 0);
+            const uint32_t bcol = smem_u32(smem + Smem::barea) + (uint32_t)(brow * stride + ((g & 1) ? kLoOff : 0));
             const int crow = (GU ? c : 4 * (dd - d0) + c) * gpr;   // column c's staged row
             float acc[2] = {0.f, 0.f};
             if (!bad) {
-                const uint8_t* tile = smem + Smem::stages + s * kStageBytes;
-                KQ<QT>::superblock(tile, p.rs, wsub, g, c, bcol, have, sums + crow, invs + crow, acc);
+                const uint32_t tile = smem_u32(smem + Smem::stages) + (uint32_t)(s * kStageBytes);
+                KQ<QT>::superblock(tile, p.rs, wsub, g, c, bcol, have, smem_u32(sums + crow), smem_u32(invs + crow), acc);
             }
             red[(s * kMaxWpt + wsub) * 32 + lane] = make_float2(acc[0], acc[1]);
             __threadfence_block();

@@ -57,6 +57,7 @@ constexpr int kBHalf = kMaxN * kKs * 2;           // 16 KB: one fp16 B operand o
 constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
 constexpr int kGridReplicas = 8;
 constexpr long long kSpinLimit = 1ll << 26;
+constexpr int kGMaxPairs = 8;                     // pairs per register-decode task (the MMA's 8 columns)
 
 struct Smem {
     static constexpr int raw = 0;                                             // the task's weight tile
@@ -485,8 +486,9 @@ struct GroupParams {
     int* cursor;      // [n_experts]
     Task* tasks;      // tcgen05 tasks: experts with >= heavy pairs
     int* n_tasks;
-    Task* mtasks;     // register-decode experts (< heavy pairs): {expert, -, first pair, pairs}; a task
-                      // is (entry, 128-row block), task index = entry * m_tiles + block
+    Task* mtasks;     // register-decode entries (experts with < heavy pairs, cut into groups of at
+                      // most kGMaxPairs): {expert, -, first pair, pairs}; a task is (entry,
+                      // 128-row block), task index = entry * m_tiles + block
     int* n_mtasks;    // entries * m_tiles
     int heavy;
     int* order;       // [pairs] pair index in grouped order
@@ -526,7 +528,7 @@ __global__ void k_group_plan(const GroupParams g) {
         const int ce = g.counts[e];
         c += ce;
         if (ce >= g.heavy) tc += (ce + kMaxN - 1) / kMaxN * g.m_tiles;
-        else if (ce > 0) mc += 1;
+        else mc += (ce + kGMaxPairs - 1) / kGMaxPairs;
     }
     s_sum[threadIdx.x] = c;
     s_tsum[threadIdx.x] = tc;
@@ -549,8 +551,8 @@ __global__ void k_group_plan(const GroupParams g) {
         if (ce >= g.heavy) {
             for (int n0 = 0; n0 < ce; n0 += kMaxN)
                 for (int mt = 0; mt < g.m_tiles; ++mt) g.tasks[tpos++] = Task{e, mt, pos + n0, min(kMaxN, ce - n0)};
-        } else if (ce > 0) {
-            g.mtasks[mpos++] = Task{e, 0, pos, ce};
+        } else {
+            for (int n0 = 0; n0 < ce; n0 += kGMaxPairs) g.mtasks[mpos++] = Task{e, 0, pos + n0, min(kGMaxPairs, ce - n0)};
         }
         pos += ce;
     }
@@ -644,7 +646,6 @@ constexpr int kGW = 8;                       // consumer warps (16 rows each: on
 constexpr int kGThreads = (kGW + 1) * 32;    // + the producer warp
 constexpr int kGTile = 16 * 880;             // a 16-row tile at k <= 2048
 constexpr int kGRep = 8;                     // grid-table replicas
-constexpr int kGMaxPairs = 8;                // pairs per expert on this kernel (more go to tcgen05)
 constexpr int kGXRow = 2048 * 2 + 32;        // bytes per staged x row (fp16, padded against bank conflicts)
 
 struct MmaSmem {
@@ -851,6 +852,20 @@ bool prefill_enabled() {
 
 }  // namespace
 
+// Experts with at least this many pairs go to the tcgen05 kernel; fewer are
+// decoded in registers, 8 pairs per task. The register path decodes a weight
+// ~4.5x faster but once per 8 pairs, the tcgen05 path once per 128. Measured
+// on B200, 512-token Zipf(1.1) prefill: 2.01 / 1.71 / 1.75 / 1.81 ms per block
+// at thresholds 9 / 25 / 33 / 49.
+static int tc_min_pairs() {
+    static int v = -1;
+    if (v < 0) {
+        const char* s = std::getenv("SABAH_IQ3S_TC_MIN_PAIRS");
+        v = s && *s ? std::max(kGMaxPairs + 1, std::atoi(s)) : 25;
+    }
+    return v;
+}
+
 // Minimum (token, slot) pairs for the grouped path: below it the decode
 // kernels, which stream each pair's tile once, are at least as fast.
 int sb_prefill_min_pairs() {
@@ -874,7 +889,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
 
     const int m_tiles = a.rows / kM;
     const long long max_tasks = (n_pairs / kMaxN + std::min<long long>(n_pairs, a.ex.n_experts) + 1) * m_tiles;
-    const long long max_mtasks = std::min<long long>(n_pairs, a.ex.n_experts);
+    const long long max_mtasks = n_pairs / kGMaxPairs + std::min<long long>(n_pairs, a.ex.n_experts) + 1;
     const long long n_xrows = (long long)a.n_tokens * a.x_rows;
     auto up256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t b_counts = up256((size_t)a.ex.n_experts * 4), b_cursor = b_counts;
@@ -922,7 +937,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
     __half* xh = (__half*)q;
     __half* xl = (__half*)(q + b_xh);
     int* xexp = (int*)(q + 2 * b_xh);
-    g.heavy = kGMaxPairs + 1;
+    g.heavy = tc_min_pairs();
     g.err = a.err;
 
     if (!g_attr_set) {

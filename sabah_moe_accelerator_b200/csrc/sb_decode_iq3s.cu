@@ -13,8 +13,11 @@
 // * Consumers wait at a grid barrier before each phase, then build the
 //   x-fragment sets of the phase's input vectors: x (gate/up) or h (down).
 // * Work is cut into units that a CTA owns whole, so every combine is local:
-//   a gate/up unit is the gate tile and the up tile of 16 rows of one (token,
-//   slot) - two items - whose last item writes h = silu(g) * u; a down unit is
+//   a gate/up unit is 32 rows (one IQ3_S sub-block of h) of one (token, slot):
+//   its two gate and two up 16-row tiles - four items - whose last item writes
+//   h = silu(g) * u and, since it holds a whole sub-block, the sub-block's
+//   x-fragment record of the down phase's set straight to global memory; the
+//   down phase then fetches a token's sets with one bulk copy. A down unit is
 //   16 rows of one token over all n_used slots, two slots per item (two bulk
 //   copies into one stage), whose last item sums the slots in slot order from
 //   shared memory and updates x in place (x += sum_e w_e v_e).
@@ -72,8 +75,8 @@ struct Smem {
     static constexpr int ucnt = cnt + kStages * 4;                     // [kUnits] ints
     static constexpr int ugen = ucnt + kUnits * 4;                     // [kUnits] ints
     static constexpr int abort_flag = ugen + kUnits * 4;
-    static constexpr int bars = (abort_flag + 4 + 7) & ~7;             // full[kStages], empty[kStages]
-    static constexpr int total = bars + 2 * kStages * 8;
+    static constexpr int bars = (abort_flag + 4 + 7) & ~7;             // full[kStages], empty[kStages], set
+    static constexpr int total = bars + (2 * kStages + 1) * 8;
 };
 static_assert(Smem::total <= 227 * 1024, "shared memory budget");
 static_assert(Smem::stages % 128 == 0 && kStageBytes % 128 == 0, "stage alignment");
@@ -106,6 +109,7 @@ struct DecodeParams {
     size_t gu_stride, dn_stride;   // bytes between experts
     float* x;                      // [T][d_model], updated in place: x += block(x) per layer
     float* h;                      // [T][n_used][ff]
+    uint8_t* hsets;                // [T][n_used] down-phase x-fragment sets of h (dn.set_stride bytes each)
     unsigned* sync;                // [0] grid-barrier arrivals, [1] exits; reset by the last CTA to exit
     int* err;
     LayerBanks layer[kMaxLayers];
@@ -142,11 +146,45 @@ __device__ inline void phase_range(const DecodeParams& p, bool down, int& i0, in
     i1 = (int)((long long)(blockIdx.x + 1) * n / gridDim.x) * G.per_unit;
 }
 
+// Lane l of a warp holds element l of sub-block j of a vector; the warp writes
+// the sub-block's x-fragment record into the vector's set at `set` (global),
+// exactly as set_put builds it in shared memory: per-sub-block power-of-two
+// scale, fp16 hi and lo parts, records (j / 4, step s) at quad j % 4, the zero
+// pairs (by quad 0) and the inverse scale.
+__device__ inline void put_record(float v, int lane, int j, uint8_t* set) {
+    float m = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int ex = 0;
+    if (m > 0.f && isfinite(m)) {
+        frexpf(m, &ex);   // m = f * 2^ex, f in [0.5, 1)
+        ex = max(-100, min(100, 14 - ex));
+    }
+    const float s = ldexpf(1.f, ex);
+    const float vs = v * s;
+    const __half hi = __float2half_rn(vs), lo = __float2half_rn(vs - __half2float(hi));
+    // pairs (2i, 2i + 1) into even lanes, then elements 4s+2, 4s+3 into lane 4s
+    const uint32_t hb = __half_as_ushort(hi), lb = __half_as_ushort(lo);
+    const uint32_t hp = hb | (__shfl_xor_sync(0xffffffffu, hb, 1) << 16);
+    const uint32_t lp = lb | (__shfl_xor_sync(0xffffffffu, lb, 1) << 16);
+    const uint32_t hp23 = __shfl_down_sync(0xffffffffu, hp, 2), lp23 = __shfl_down_sync(0xffffffffu, lp, 2);
+    const int q = j >> 2, c = j & 3, st = lane >> 2;
+    uint8_t* grp = set + q * kGroupBytes;
+    if ((lane & 3) == 0) {
+        uint2* rec = (uint2*)(grp + st * kRecBytes);
+        rec[2 * c] = make_uint2(hp, hp23);
+        rec[2 * c + 1] = make_uint2(lp, lp23);
+        if (c == 0) rec[8] = make_uint2(0, 0);
+    }
+    // 2^24 undoes the subnormal encoding of the weights, 1/s the x scale
+    if (lane == 0) ((float*)(grp + 8 * kRecBytes))[c] = 16777216.0f / s;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* bars = (uint64_t*)(smem + Smem::bars);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages), setbar = smem_u32(bars + 2 * kStages);
     volatile int* abort_flag = (volatile int*)(smem + Smem::abort_flag);
     Desc* descs = (Desc*)(smem + Smem::desc);
     const int n_phases = 2 * p.n_layers;
@@ -157,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);   // one release per item, by its last warp
         }
+        mbar_init(setbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (threadIdx.x < kStages) {
@@ -194,10 +233,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                     const uint8_t* src[2] = {nullptr, nullptr};
                     d.bad = 0;
                     if (!down) {
-                        d.which = item & 1;
-                        const int r = item >> 1;
-                        d.rt = r % G.rtiles;
-                        const int si = r / G.rtiles;
+                        // unit (token, slot, 32-row block): gate 0-15, up 0-15, gate 16-31, up 16-31
+                        const int unit = item >> 2, part = item & 3;
+                        d.which = part & 1;
+                        const int si = unit / (G.rtiles / 2);
+                        d.rt = 2 * (unit % (G.rtiles / 2)) + (part >> 1);
                         d.t = si / p.n_used;
                         d.e = si % p.n_used;
                         d.n = 1;
@@ -254,6 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
     uint8_t* sets = smem + Smem::sets;
     const DecodeParams* pp = &p;
     int seq_base = 0;
+    int set_copies = 0;   // bulk copies of down-phase sets issued (thread 0) and waited for
 
     for (int ph = 0; ph < n_phases; ++ph) {
         // grid barrier: the previous phase's rows (or x) are all written
@@ -302,12 +343,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
             if (item > i0) consumers_sync();   // every warp is done with the previous chunk's sets
             const int sst = G.set_stride;
             if (down) {
-                // h of (token, slot e) into set e
-                auto load_h = [pp, key0](int i, int f) {
-                    return __ldcg((const float4*)(pp->h + (size_t)(key0 + i) * pp->ff) + f);
-                };
-                auto set_e = [sets, sst](int i) { return sets + i * sst; };
-                build_sets_from<kNC * 32, decltype(load_h), decltype(set_e), 4>(n_keys, load_h, set_e, G.k);
+                // the token's n_used sets, written by the gate/up units, in one bulk copy.
+                // The generic-proxy writes of other CTAs (released at the grid barrier,
+                // acquired by thread 0) are ordered before this async-proxy read, and the
+                // set area's earlier generic reads before its overwrite, by the proxy fence.
+                if (threadIdx.x == 0) {
+                    asm volatile("fence.proxy.async;" ::: "memory");
+                    const uint32_t bytes = (uint32_t)(n_keys * sst);
+                    mbar_expect_tx(setbar, bytes);
+                    bulk_g2s(sets32, p.hsets + (size_t)key0 * sst, bytes, setbar);
+                }
+                mbar_wait(setbar, set_copies & 1, p.err, abort_flag);   // on timeout the items see the abort
+                ++set_copies;
             } else {
                 build_sets_from<kNC * 32>(
                     n_keys,
@@ -395,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                 __threadfence_block();
                 float* ubase = ubuf + ub * kMaxUsed * 16;
                 if (!down) {
-                    if (lane < 16) ubase[d.which * 16 + lane] = v;   // gate rows, up rows
+                    if (lane < 16) ubase[(d.which * 2 + (d.rt & 1)) * 16 + lane] = v;   // gate rows, up rows
                 } else {
                     const int tl = lane >> 4, e = d.e + tl;
                     if (tl < d.n) ubase[e * 16 + (lane & 15)] = __ldg(p.layer[layer].w + d.t * p.n_used + e) * v;
@@ -410,17 +457,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                 ulast = __shfl_sync(0xffffffffu, ulast, 0);
                 if (!ulast) continue;
                 __threadfence_block();
-                if (lane < 16) {
-                    if (!down) {
-                        const float gv = ubase[lane], uv = ubase[16 + lane];
-                        p.h[((size_t)d.t * p.n_used + d.e) * p.ff + d.rt * 16 + lane] = gv / (1.f + expf(-gv)) * uv;
-                    } else {
-                        // the top-k weighted sum in slot order, then the residual
-                        float tot = 0.f;
-                        for (int e2 = 0; e2 < p.n_used; ++e2) tot += ubase[e2 * 16 + lane];
-                        float* o = p.x + (size_t)d.t * p.d_model + d.rt * 16 + lane;
-                        *o = __ldcg(o) + tot;
-                    }
+                if (!down) {
+                    // h of the unit's 32 rows (one sub-block), then its set record
+                    const size_t si = (size_t)d.t * p.n_used + d.e;
+                    const int half = lane >> 4, r16 = lane & 15, j = d.rt >> 1;
+                    const float gv = ubase[half * 16 + r16], uv = ubase[(2 + half) * 16 + r16];
+                    const float hv = gv / (1.f + expf(-gv)) * uv;
+                    p.h[si * p.ff + 32 * j + lane] = hv;
+                    put_record(hv, lane, j, p.hsets + si * p.dn.set_stride);
+                } else if (lane < 16) {
+                    // the top-k weighted sum in slot order, then the residual
+                    float tot = 0.f;
+                    for (int e2 = 0; e2 < p.n_used; ++e2) tot += ubase[e2 * 16 + lane];
+                    float* o = p.x + (size_t)d.t * p.d_model + d.rt * 16 + lane;
+                    *o = __ldcg(o) + tot;
                 }
                 __syncwarp();
                 __threadfence_block();
@@ -430,6 +480,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
         }
         seq_base += i1 - i0;
     }
+    // never leave with a set copy in flight (its wait may have given up)
+    if (threadIdx.x == 0 && set_copies > 0)
+        for (long long i = 0; i < kSpinLimit && !mbar_try_wait(setbar, (set_copies - 1) & 1); ++i) {
+        }
     // the last CTA out resets the barrier words for the next launch
     consumers_sync();
     if (threadIdx.x == 0) {
@@ -504,7 +558,7 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     if (((uintptr_t)a.h & 15)) return 0;
     p.gu.n_items = (int)gu_items;
     p.gu.per_key = a.n_used * p.gu.rtiles * 2;   // items of one token
-    p.gu.per_unit = 2;                           // gate tile + up tile of 16 rows
+    p.gu.per_unit = 4;                           // gate and up tiles of 32 rows (one sub-block of h)
     p.dn.n_items = (int)dn_items;
     p.dn.per_key = p.dn.rtiles * pairs;          // items of one token
     p.dn.per_unit = pairs;                       // 16 rows over all slots
@@ -524,10 +578,11 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     }
     if (g_grid < 1) return 0;
 
-    // scratch: the barrier words (zeroed, self-resetting)
+    // scratch: the barrier words (zeroed, self-resetting), then the down-phase sets of h
     const size_t sync_b = 256;
-    if (sync_b > g_ds.counter_cap) {
-        const size_t ccap = sync_b, pcap = 0;
+    const size_t sets_b = (size_t)a.n_tokens * a.n_used * p.dn.set_stride;
+    if (sync_b > g_ds.counter_cap || sets_b > g_ds.partial_cap) {
+        const size_t ccap = std::max(sync_b, g_ds.counter_cap), pcap = std::max(sets_b, g_ds.partial_cap);
         if (g_ds.mem) {
             cudaDeviceSynchronize();   // no kernel of an earlier call may still use it
             cudaFree(g_ds.mem);
@@ -544,6 +599,7 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     }
     uint8_t* b = (uint8_t*)g_ds.mem;
     p.sync = (unsigned*)b;
+    p.hsets = b + g_ds.counter_cap;
 
     p.n_layers = a.n_layers;
     p.n_tokens = a.n_tokens;

@@ -93,6 +93,7 @@ struct Geo {
     int wpt, tpw;    // warps per item, tasks per warp
     int k, rb;       // row length, row bytes
     int set_stride;  // bytes of one x-fragment set (k / 128 groups)
+    int rowpair;     // down with one slot: an item is 32 rows (two row tiles) of that slot
 };
 
 struct LayerBanks {
@@ -107,7 +108,9 @@ struct DecodeParams {
     Geo gu, dn;
     int n_layers, n_tokens, n_used, n_experts, d_model, ff;
     size_t gu_stride, dn_stride;   // bytes between experts
-    float* x;                      // [T][d_model], updated in place: x += block(x) per layer
+    float* x;                      // [T][d_model]: the blocks' input (x += block(x) per layer when out == x)
+    float* out;                    // the combine's destination: out = (accumulate ? out : 0) + y
+    int accumulate;
     float* h;                      // [T][n_used][ff]
     uint8_t* hsets;                // [T][n_used] down-phase x-fragment sets of h (dn.set_stride bytes each)
     unsigned* sync;                // [0] grid-barrier arrivals, [1] exits; reset by the last CTA to exit
@@ -245,14 +248,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                         src[0] = expert_row_tile(p, lb, d.which, si, d.rt, d.e);
                     } else {
                         d.which = 0;
-                        const int unit = item / G.per_unit, pair = item % G.per_unit;
-                        d.t = unit / G.rtiles;
-                        d.rt = unit % G.rtiles;
-                        d.e = 2 * pair;
-                        d.n = min(2, p.n_used - d.e);
-                        d.slot = d.e;
-                        for (int tl = 0; tl < d.n; ++tl)
-                            src[tl] = expert_row_tile(p, lb, 2, d.t * p.n_used + d.e + tl, d.rt, d.e + tl);
+                        if (G.rowpair) {
+                            // one slot: the unit (and item) is 32 rows, row tiles 2rb and 2rb + 1
+                            d.t = item / (G.rtiles / 2);
+                            d.rt = 2 * (item % (G.rtiles / 2));
+                            d.e = 0;
+                            d.n = 2;
+                            d.slot = 0;
+                            for (int tl = 0; tl < 2; ++tl)
+                                src[tl] = expert_row_tile(p, lb, 2, d.t * p.n_used, d.rt + tl, 0);
+                        } else {
+                            const int unit = item / G.per_unit, pair = item % G.per_unit;
+                            d.t = unit / G.rtiles;
+                            d.rt = unit % G.rtiles;
+                            d.e = 2 * pair;
+                            d.n = min(2, p.n_used - d.e);
+                            d.slot = d.e;
+                            for (int tl = 0; tl < d.n; ++tl)
+                                src[tl] = expert_row_tile(p, lb, 2, d.t * p.n_used + d.e + tl, d.rt, d.e + tl);
+                        }
                     }
                     for (int tl = 0; tl < d.n; ++tl)
                         if (!d.bad) d.bad = !src[tl] ? SB_DERR_BAD_ID : ((uintptr_t)src[tl] & 15) ? SB_DERR_MISALIGNED : 0;
@@ -378,7 +392,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                         const int tl = j / G.ppr, q = 2 * (j - tl * G.ppr);
                         if (tl >= d.n) break;
                         float r[2] = {0.f, 0.f};
-                        do_pair<kLogR>(tile0 + (uint32_t)(tl * 16 * G.rb), q, sets32 + (d.slot + tl) * sst + boff, L, r);
+                        const int set = d.slot + (G.rowpair ? 0 : tl);
+                        do_pair<kLogR>(tile0 + (uint32_t)(tl * 16 * G.rb), q, sets32 + set * sst + boff, L, r);
                         acc[0][0] += tl ? 0.f : r[0];
                         acc[0][1] += tl ? 0.f : r[1];
                         acc[1][0] += tl ? r[0] : 0.f;
@@ -444,8 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                 if (!down) {
                     if (lane < 16) ubase[(d.which * 2 + (d.rt & 1)) * 16 + lane] = v;   // gate rows, up rows
                 } else {
-                    const int tl = lane >> 4, e = d.e + tl;
-                    if (tl < d.n) ubase[e * 16 + (lane & 15)] = __ldg(p.layer[layer].w + d.t * p.n_used + e) * v;
+                    // row pair: buffer rows 0..31 of the single slot; else 16 rows per slot
+                    const int tl = lane >> 4, e = G.rowpair ? d.e : d.e + tl;
+                    if (tl < d.n)
+                        ubase[(G.rowpair ? tl : e) * 16 + (lane & 15)] = __ldg(p.layer[layer].w + d.t * p.n_used + e) * v;
                 }
                 __threadfence_block();
                 __syncwarp();
@@ -465,12 +482,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                     const float hv = gv / (1.f + expf(-gv)) * uv;
                     p.h[si * p.ff + 32 * j + lane] = hv;
                     put_record(hv, lane, j, p.hsets + si * p.dn.set_stride);
+                } else if (G.rowpair) {
+                    // one slot, 32 rows
+                    const float tot = ubase[lane];
+                    float* o = p.out + (size_t)d.t * p.d_model + d.rt * 16 + lane;
+                    *o = p.accumulate ? __ldcg(o) + tot : tot;
                 } else if (lane < 16) {
                     // the top-k weighted sum in slot order, then the residual
                     float tot = 0.f;
                     for (int e2 = 0; e2 < p.n_used; ++e2) tot += ubase[e2 * 16 + lane];
-                    float* o = p.x + (size_t)d.t * p.d_model + d.rt * 16 + lane;
-                    *o = __ldcg(o) + tot;
+                    float* o = p.out + (size_t)d.t * p.d_model + d.rt * 16 + lane;
+                    *o = p.accumulate ? __ldcg(o) + tot : tot;
                 }
                 __syncwarp();
                 __threadfence_block();
@@ -547,21 +569,25 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     DecodeParams p{};
     if (!plan(a.d_model, a.ff, 1, p.gu) || !plan(a.ff, a.d_model, 2, p.dn)) return 0;
     if (kGuSets * p.gu.set_stride > kSetArea || a.n_used * p.dn.set_stride > kSetArea) return 0;
-    if (a.gu_expert_stride % 16 || a.down_expert_stride % 16 || ((uintptr_t)a.x & 15)) return 0;
+    if (a.gu_expert_stride % 16 || a.down_expert_stride % 16 || ((uintptr_t)a.x & 15) || !a.out) return 0;
+    if (a.n_layers > 1 && (a.out != a.x || !a.accumulate)) return 0;   // the residual chain
+    if ((long long)a.n_tokens * a.n_used > 16384) return 0;
     for (int L = 0; L < a.n_layers; ++L)
         for (const void* b : {a.gate_banks[L], a.up_banks[L], a.down_banks[L]})
             if (!b || ((uintptr_t)b & 15)) return 0;
     const long long gu_items = (long long)a.n_tokens * a.n_used * p.gu.rtiles * 2;
     const int pairs = (a.n_used + 1) / 2;
-    const long long dn_items = (long long)a.n_tokens * p.dn.rtiles * pairs;
+    p.dn.rowpair = a.n_used == 1 && p.dn.rtiles % 2 == 0;
+    const long long dn_items = p.dn.rowpair ? (long long)a.n_tokens * (p.dn.rtiles / 2)
+                                            : (long long)a.n_tokens * p.dn.rtiles * pairs;
     if (gu_items > (1 << 28) || dn_items > (1 << 28)) return 0;
     if (((uintptr_t)a.h & 15)) return 0;
     p.gu.n_items = (int)gu_items;
     p.gu.per_key = a.n_used * p.gu.rtiles * 2;   // items of one token
     p.gu.per_unit = 4;                           // gate and up tiles of 32 rows (one sub-block of h)
     p.dn.n_items = (int)dn_items;
-    p.dn.per_key = p.dn.rtiles * pairs;          // items of one token
-    p.dn.per_unit = pairs;                       // 16 rows over all slots
+    p.dn.per_key = p.dn.rowpair ? p.dn.rtiles / 2 : p.dn.rtiles * pairs;   // items of one token
+    p.dn.per_unit = p.dn.rowpair ? 1 : pairs;    // 32 rows of one slot, or 16 rows over all slots
 
     if (!g_attr_set) {
         if (!sb_cuda_ok(cudaFuncSetAttribute(k_decode_iq3s, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total),
@@ -610,6 +636,8 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     p.gu_stride = a.gu_expert_stride;
     p.dn_stride = a.down_expert_stride;
     p.x = a.x;
+    p.out = a.out;
+    p.accumulate = a.accumulate;
     p.h = a.h;
     p.err = a.err;
     const size_t per_layer = (size_t)a.n_tokens * a.n_used;

@@ -94,8 +94,10 @@ struct sb_decode_args {
     int n_experts;
     const int32_t* ids;
     const float* w;
-    float* x;
+    float* x;                // [n_tokens][d_model]: the input of block 0
     float* h;
+    float* out;              // the last block's destination: out = (accumulate ? out : 0) + y; must be x
+    int accumulate;          // when n_layers > 1 (the residual chain x += y)
     int d_model, ff, n_used, n_tokens;
     int qt_gate, qt_up, qt_down;
     int* err;

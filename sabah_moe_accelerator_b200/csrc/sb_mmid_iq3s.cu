@@ -513,6 +513,39 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !fast_path_enabled()) return 0;
     const int grouped = sb_block_iq3s_grouped(a, st);   // many (token, slot) pairs
     if (grouped != 0) return grouped;
+    // one persistent launch (sb_decode_iq3s.cu, one block): every combine is CTA-local,
+    // so it has none of the cross-CTA hand-offs of the two launches below
+    if (!a.gate.ptrs && !a.up.ptrs && !a.down.ptrs && a.gate.ids && a.gate.ids == a.up.ids &&
+        a.gate.ids == a.down.ids && a.gate.ids_id_stride == 4 && a.gate.ids_token_stride == (size_t)4 * a.n_used &&
+        a.gate.expert_stride == a.up.expert_stride && a.gate.n_experts == a.down.n_experts) {
+        const void* gb = a.gate.base;
+        const void* ub = a.up.base;
+        const void* db = a.down.base;
+        sb_decode_args d{};
+        d.n_layers = 1;
+        d.gate_banks = &gb;
+        d.up_banks = &ub;
+        d.down_banks = &db;
+        d.gu_expert_stride = a.gate.expert_stride;
+        d.down_expert_stride = a.down.expert_stride;
+        d.n_experts = a.gate.n_experts;
+        d.ids = a.gate.ids;
+        d.w = a.w;
+        d.x = const_cast<float*>(a.x);   // read only: with one block the combine goes to out
+        d.h = a.h;
+        d.out = a.out;
+        d.accumulate = a.accumulate;
+        d.d_model = a.d_model;
+        d.ff = a.ff;
+        d.n_used = a.n_used;
+        d.n_tokens = a.n_tokens;
+        d.qt_gate = a.qt_gate;
+        d.qt_up = a.qt_up;
+        d.qt_down = a.qt_down;
+        d.err = a.err;
+        const int taken = sb_try_decode_iq3s(d, st);
+        if (taken != 0) return taken;
+    }
     int wpt_g, gpw_g, wpt_d, gpw_d;
     if (!plan_groups(a.d_model, wpt_g, gpw_g) || !plan_groups(a.ff, wpt_d, gpw_d)) return 0;
     if (a.ff % 16 || a.d_model % 16) return 0;

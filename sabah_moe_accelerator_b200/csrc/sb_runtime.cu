@@ -1418,6 +1418,8 @@ SABAH_API int sabah_moe_decode(int n_layers, const void* const* gate_banks, cons
         a.w = d_w;
         a.x = d_x;
         a.h = d_h;
+        a.out = d_x;
+        a.accumulate = 1;
         a.d_model = d_model;
         a.ff = ff;
         a.n_used = n_used;

@@ -139,3 +139,30 @@ def test_block_ids_grouped_path(gpu_rt, orc, T):
     ops.moe_block_ids(gate, up, down, ids_d, w_d, x_d, d_model, ff, E, qt, qt, qt, out=out, accumulate=True)
     torch.cuda.synchronize()
     assert orc.rel_l2(out.cpu().numpy(), 2 * got) <= TIGHT
+
+
+@pytest.mark.parametrize("T,E", [(80, 64), (7, 16)])
+def test_block_ids_one_slot_per_token(gpu_rt, orc, T, E):
+    """n_used = 1 (the expert-parallel bank's per-pair call): the one-launch path
+    takes 32 down rows of the single slot per item; against fp64, accumulate."""
+    from sabah_moe_accelerator_b200 import ops
+    d_model, ff, qt = 2048, 768, 21
+    gate = ops.synth_rows(E * ff, d_model, qt, seed=71, sigma=0.02)
+    up = ops.synth_rows(E * ff, d_model, qt, seed=72, sigma=0.02)
+    down = ops.synth_rows(E * d_model, ff, qt, seed=73, sigma=0.02)
+    rng = np.random.default_rng(T)
+    ids = rng.integers(0, E, (T, 1)).astype(np.int32)
+    w = (rng.random((T, 1)) + 0.5).astype(np.float32)
+    x = rng.standard_normal((T, d_model)).astype(np.float32)
+    ids_d, w_d, x_d = torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()
+    out = ops.moe_block_ids(gate, up, down, ids_d, w_d, x_d, d_model, ff, E, qt, qt, qt)
+    got = out.cpu().numpy()
+    g, u, d = (b.cpu().numpy().reshape(E, -1) for b in (gate, up, down))
+    for t in sorted({0, T // 2, T - 1}):
+        want = orc.moe_block_f64(g, u, d, ids[t], w[t], x[t], d_model, ff, qt, qt, qt)
+        r = orc.rel_l2(got[t], want)
+        assert r <= TOL and r <= TIGHT, (t, r)
+    acc = x_d.clone()
+    ops.moe_block_ids(gate, up, down, ids_d, w_d, x_d, d_model, ff, E, qt, qt, qt, out=acc, accumulate=True)
+    torch.cuda.synchronize()
+    assert orc.rel_l2(acc.cpu().numpy(), x + got) <= TIGHT

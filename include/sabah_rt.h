@@ -80,6 +80,19 @@ int sabah_moe_block_ids(const void *gate_bank, const void *up_bank, const void *
                         int n_used, int n_tokens, int qt_gate, int qt_up, int qt_down, int accumulate,
                         void *stream);
 
+/* sabah_moe_block_ids over gathered inputs. No reference counterpart.
+ * Token t's input is row d_xrows[t] of d_x, which has n_xrows rows of d_model
+ * floats; everything else is as sabah_moe_block_ids. The expert-parallel bank
+ * (sharded experts, one process per GPU) calls it with the all-gathered
+ * activations and, per local (token, slot) pair, the pair's token row, so no
+ * separate gather pass runs. A row index outside [0, n_xrows) gives NaN
+ * outputs for that token and the device error (sabah_rt_device_error). */
+int sabah_moe_block_gather(const void *gate_bank, const void *up_bank, const void *down_bank,
+                           size_t gu_expert_stride, size_t down_expert_stride, int n_experts, const int32_t *d_ids,
+                           const float *d_w, const float *d_x, const int32_t *d_xrows, int n_xrows, float *d_out,
+                           float *d_h, int d_model, int ff, int n_used, int n_tokens, int qt_gate, int qt_up,
+                           int qt_down, int accumulate, void *stream);
+
 /* sabah_moe_block_ids without any allocation. No reference counterpart.
  * sabah_moe_block_ids grows its cross-CTA scratch with cudaMalloc the first
  * time it meets a larger shape, which some callers cannot allow: code being

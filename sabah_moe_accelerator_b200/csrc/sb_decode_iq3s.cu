@@ -111,6 +111,8 @@ struct DecodeParams {
     float* x;                      // [T][d_model]: the blocks' input (x += block(x) per layer when out == x)
     float* out;                    // the combine's destination: out = (accumulate ? out : 0) + y
     int accumulate;
+    const int32_t* xrows;          // one block: token t's input is row xrows[t] of x (nullptr: row t)
+    int n_xrows;
     float* h;                      // [T][n_used][ff]
     uint8_t* hsets;                // [T][n_used] down-phase x-fragment sets of h (dn.set_stride bytes each)
     unsigned* sync;                // [0] grid-barrier arrivals, [1] exits; reset by the last CTA to exit
@@ -373,7 +375,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode_iq3s(const __grid_consta
                 build_sets_from<kNC * 32>(
                     n_keys,
                     [pp, key0](int i, int f) {
-                        return __ldcg((const float4*)(pp->x + (size_t)(key0 + i) * pp->d_model) + f);
+                        int r = key0 + i;
+                        if (pp->xrows) {
+                            r = __ldg(pp->xrows + r);
+                            if (r < 0 || r >= pp->n_xrows) {   // no such row: NaN outputs, error recorded
+                                if (f == 0 && pp->err) atomicExch(pp->err, SB_DERR_BAD_ID);
+                                const float nan = __int_as_float(0x7fc00000);
+                                return make_float4(nan, nan, nan, nan);
+                            }
+                        }
+                        return __ldcg((const float4*)(pp->x + (size_t)r * pp->d_model) + f);
                     },
                     [sets, sst, key0](int i) { return sets + ((key0 + i) % kGuSets) * sst; }, G.k);
             }
@@ -570,7 +581,7 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     if (!plan(a.d_model, a.ff, 1, p.gu) || !plan(a.ff, a.d_model, 2, p.dn)) return 0;
     if (kGuSets * p.gu.set_stride > kSetArea || a.n_used * p.dn.set_stride > kSetArea) return 0;
     if (a.gu_expert_stride % 16 || a.down_expert_stride % 16 || ((uintptr_t)a.x & 15) || !a.out) return 0;
-    if (a.n_layers > 1 && (a.out != a.x || !a.accumulate)) return 0;   // the residual chain
+    if (a.n_layers > 1 && (a.out != a.x || !a.accumulate || a.xrows)) return 0;   // the residual chain
     if ((long long)a.n_tokens * a.n_used > 16384) return 0;
     for (int L = 0; L < a.n_layers; ++L)
         for (const void* b : {a.gate_banks[L], a.up_banks[L], a.down_banks[L]})
@@ -638,6 +649,8 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     p.x = a.x;
     p.out = a.out;
     p.accumulate = a.accumulate;
+    p.xrows = a.xrows;
+    p.n_xrows = a.n_xrows;
     p.h = a.h;
     p.err = a.err;
     const size_t per_layer = (size_t)a.n_tokens * a.n_used;

@@ -28,13 +28,20 @@ int sm_count() {
 // one thread per float4 of the output, at most 8 CTAs per SM
 int grid_elems(long long n4) { return (int)std::max(1LL, std::min((n4 + kThreads - 1) / kThreads, 8LL * sm_count())); }
 
-// dst[i] = src[rows[i]]; a row index outside [0, n_src) gives a zero row
-__global__ void k_gather_rows(const float4* src, int n_src, const int32_t* rows, int n, int k4, float4* dst) {
+// dst[i] = src[rows[i]]; a row index outside [0, n_src) gives a zero row, or,
+// with err, a NaN row and SB_DERR_BAD_ID in *err
+__global__ void k_gather_rows(const float4* src, int n_src, const int32_t* rows, int n, int k4, float4* dst, int* err) {
     const long long total = (long long)n * k4;
     for (long long q = blockIdx.x * (long long)kThreads + threadIdx.x; q < total; q += (long long)gridDim.x * kThreads) {
         const int i = (int)(q / k4), j = (int)(q % k4);
         const int r = __ldg(rows + i);
-        dst[q] = (r < 0 || r >= n_src) ? make_float4(0.f, 0.f, 0.f, 0.f) : __ldg(src + (size_t)r * k4 + j);
+        if (r < 0 || r >= n_src) {
+            const float f = err ? __int_as_float(0x7fc00000) : 0.f;
+            if (err && j == 0) atomicExch(err, SB_DERR_BAD_ID);
+            dst[q] = make_float4(f, f, f, f);
+        } else {
+            dst[q] = __ldg(src + (size_t)r * k4 + j);
+        }
     }
 }
 
@@ -82,6 +89,14 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 }  // namespace
 
+int sb_gather_rows(const float* src, int n_src, const int32_t* rows, int n, int k, float* dst, int* err,
+                   cudaStream_t st) {
+    if (n <= 0) return 0;
+    k_gather_rows<<<grid_elems((long long)n * (k / 4)), kThreads, 0, st>>>((const float4*)src, n_src, rows, n, k / 4,
+                                                                         (float4*)dst, err);
+    return sb_cuda_ok(cudaGetLastError(), "gather launch") ? 0 : -1;
+}
+
 SABAH_API int sabah_ep_gather_rows(const float* d_src, int n_src, const int32_t* d_rows, int n, int k,
                                    float* d_dst, void* stream) {
     if (n < 0 || n_src < 0 || k <= 0 || k % 4 || (n > 0 && (!d_src || !d_rows || !d_dst)) || !aligned16(d_src) ||
@@ -92,7 +107,7 @@ SABAH_API int sabah_ep_gather_rows(const float* d_src, int n_src, const int32_t*
     if (n == 0) return 0;
     const int tslot = sb_timing_begin("ep_gather_rows", (cudaStream_t)stream);
     k_gather_rows<<<grid_elems((long long)n * (k / 4)), kThreads, 0, (cudaStream_t)stream>>>(
-        (const float4*)d_src, n_src, d_rows, n, k / 4, (float4*)d_dst);
+        (const float4*)d_src, n_src, d_rows, n, k / 4, (float4*)d_dst, nullptr);
     sb_timing_end(tslot, (cudaStream_t)stream);
     return sb_cuda_ok(cudaGetLastError(), "ep gather launch") ? 0 : -1;
 }

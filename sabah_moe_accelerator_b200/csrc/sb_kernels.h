@@ -50,6 +50,8 @@ struct sb_block_args {
     int qt_gate, qt_up, qt_down;
     int accumulate;                // out += y instead of out = y
     int* err;
+    const int32_t* xrows;          // optional: token t's input is row xrows[t] of x (nullptr: row t)
+    int n_xrows;                   // rows of x when xrows is given
 };
 
 // device-side error codes written to *err
@@ -79,6 +81,10 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);
 // Q4_K / Q6_K fused block for 1-4 tokens on device banks, each distinct routed
 // expert decoded once per block (sb_small_kq.cu): 1 taken, 0 not covered, -1 error
 int sb_try_block_small(const sb_block_args& a, cudaStream_t st);
+// sb_ep.cu: dst[i] = src[rows[i]]; indices outside [0, n_src) give NaN rows and
+// SB_DERR_BAD_ID in *err (zero rows when err is null)
+int sb_gather_rows(const float* src, int n_src, const int32_t* rows, int n, int k, float* dst, int* err,
+                   cudaStream_t st);
 // After a device error: the fused block's cross-CTA arrival counters may have
 // been left mid-count by a kernel that gave up; the next call clears them.
 void sb_block_scratch_invalidate();
@@ -98,6 +104,8 @@ struct sb_decode_args {
     float* h;
     float* out;              // the last block's destination: out = (accumulate ? out : 0) + y; must be x
     int accumulate;          // when n_layers > 1 (the residual chain x += y)
+    const int32_t* xrows;    // one block only, optional: token t's input is row xrows[t] of x
+    int n_xrows;
     int d_model, ff, n_used, n_tokens;
     int qt_gate, qt_up, qt_down;
     int* err;

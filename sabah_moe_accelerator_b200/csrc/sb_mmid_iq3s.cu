@@ -511,8 +511,10 @@ int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
 
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !fast_path_enabled()) return 0;
-    const int grouped = sb_block_iq3s_grouped(a, st);   // many (token, slot) pairs
-    if (grouped != 0) return grouped;
+    if (!a.xrows) {   // the grouped path reads rows t only
+        const int grouped = sb_block_iq3s_grouped(a, st);   // many (token, slot) pairs
+        if (grouped != 0) return grouped;
+    }
     // one persistent launch (sb_decode_iq3s.cu, one block): every combine is CTA-local,
     // so it has none of the cross-CTA hand-offs of the two launches below
     if (!a.gate.ptrs && !a.up.ptrs && !a.down.ptrs && a.gate.ids && a.gate.ids == a.up.ids &&
@@ -535,6 +537,8 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
         d.h = a.h;
         d.out = a.out;
         d.accumulate = a.accumulate;
+        d.xrows = a.xrows;
+        d.n_xrows = a.n_xrows;
         d.d_model = a.d_model;
         d.ff = a.ff;
         d.n_used = a.n_used;
@@ -546,6 +550,7 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
         const int taken = sb_try_decode_iq3s(d, st);
         if (taken != 0) return taken;
     }
+    if (a.xrows) return 0;   // the launches below read rows t only
     int wpt_g, gpw_g, wpt_d, gpw_d;
     if (!plan_groups(a.d_model, wpt_g, gpw_g) || !plan_groups(a.ff, wpt_d, gpw_d)) return 0;
     if (a.ff % 16 || a.d_model % 16) return 0;

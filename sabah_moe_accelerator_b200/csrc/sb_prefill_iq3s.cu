@@ -1029,11 +1029,12 @@ BlockGroupedScratch g_bgs;
 // Whether the fused block runs grouped. SABAH_IQ3S_BLOCK_GROUPED_MIN fixes a
 // pair threshold; by default a cost model chooses, fitted on B200 (2048 x 768
 // IQ3_S experts, uniform routing, 64 and 512 experts, 1-1024 pairs): the
-// one-launch per-pair path costs ~1.4 us a pair; the grouped path ~145 us plus
-// ~2 us per distinct expert and 8-pair task, with the distinct experts of P
-// uniformly routed pairs over E expected at E (1 - exp(-P / E)). The ids are on
-// the device, so the expectation stands in for the count.
-bool block_grouped_wins(long long pairs, int n_experts) {
+// one-launch path costs ~20 us plus ~1.1 us a pair with one slot per token
+// (32-row down items) and ~1.4 us a pair otherwise; the grouped path ~145 us
+// plus ~2 us per distinct expert and 8-pair task, with the distinct experts of
+// P uniformly routed pairs over E expected at E (1 - exp(-P / E)). The ids are
+// on the device, so the expectation stands in for the count.
+bool block_grouped_wins(long long pairs, int n_experts, int n_used) {
     static int v = -1;
     if (v < 0) {
         const char* s = std::getenv("SABAH_IQ3S_BLOCK_GROUPED_MIN");
@@ -1043,7 +1044,7 @@ bool block_grouped_wins(long long pairs, int n_experts) {
     const double P = (double)pairs, E = (double)std::max(1, n_experts);
     const double distinct = E * (1.0 - std::exp(-P / E));
     const double tasks = distinct * std::max(1.0, std::ceil(P / distinct / 8.0));
-    return 145.0 + 2.0 * tasks < 1.4 * P;
+    return 145.0 + 2.0 * tasks < (n_used == 1 ? 20.0 + 1.1 * P : 1.4 * P);
 }
 
 }  // namespace
@@ -1051,7 +1052,7 @@ bool block_grouped_wins(long long pairs, int n_experts) {
 int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !prefill_enabled()) return 0;
     const long long slots = (long long)a.n_tokens * a.n_used;
-    if (!block_grouped_wins(slots, a.gate.n_experts) || slots > (1 << 22)) return 0;
+    if (!block_grouped_wins(slots, a.gate.n_experts, a.n_used) || slots > (1 << 22)) return 0;
     if (a.gate.ptrs || a.up.ptrs || a.down.ptrs) return 0;
     if (a.d_model % 256 || a.ff % 256 || a.d_model > 2048 || a.ff > 2048 || a.d_model % kM || a.ff % kM) return 0;
     for (const sb_experts* e : {&a.gate, &a.up, &a.down})

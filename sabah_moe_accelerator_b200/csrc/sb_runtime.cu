@@ -953,6 +953,88 @@ SABAH_API int sabah_moe_block_ids(const void* gate_bank, const void* up_bank, co
     return sb_launch_block(a, stream ? (cudaStream_t)stream : g_rt.compute);
 }
 
+// sabah_moe_block_ids over gathered inputs: token t's input is row d_xrows[t]
+// of d_x (n_xrows rows). No reference counterpart: the expert-parallel bank
+// calls it with the all-gathered activations and the rows of its local
+// (token, slot) pairs. IQ3_S blocks that take the one-launch path read the
+// rows in place; every other case gathers them into scratch first. A row index
+// outside [0, n_xrows) gives NaN outputs and the device error.
+SABAH_API int sabah_moe_block_gather(const void* gate_bank, const void* up_bank, const void* down_bank,
+                                     size_t gu_expert_stride, size_t down_expert_stride, int n_experts,
+                                     const int32_t* d_ids, const float* d_w, const float* d_x, const int32_t* d_xrows,
+                                     int n_xrows, float* d_out, float* d_h, int d_model, int ff, int n_used,
+                                     int n_tokens, int qt_gate, int qt_up, int qt_down, int accumulate, void* stream) {
+    if (!ensure_init()) return -1;
+    if (!device_errors_clear()) return -1;
+    if (!gate_bank || !up_bank || !down_bank || !d_ids || !d_w || !d_x || !d_xrows || !d_out || !d_h ||
+        n_xrows <= 0) {
+        sb_set_error("invalid moe_block_gather arguments");
+        return -1;
+    }
+    if ((d_model % 32) || (ff % 32) || n_used <= 0 || n_tokens < 0 || n_experts <= 0) {
+        sb_set_error("invalid moe_block_gather geometry");
+        return -1;
+    }
+    if (!sb_row_bytes_of(qt_gate, d_model) || !sb_row_bytes_of(qt_up, d_model) || !sb_row_bytes_of(qt_down, ff)) {
+        sb_set_error("unsupported quant type or row length for the block (%d/%d/%d)", qt_gate, qt_up, qt_down);
+        return -1;
+    }
+    if (n_tokens == 0) return 0;
+    const cudaStream_t st = stream ? (cudaStream_t)stream : g_rt.compute;
+    sb_block_args a{};
+    auto bank = [&](const void* b, size_t stride) {
+        sb_experts e{};
+        e.base = (const uint8_t*)b;
+        e.expert_stride = stride;
+        e.ids = d_ids;
+        e.ids_id_stride = 4;
+        e.ids_token_stride = (size_t)4 * n_used;
+        e.n_experts = n_experts;
+        return e;
+    };
+    a.gate = bank(gate_bank, gu_expert_stride);
+    a.up = bank(up_bank, gu_expert_stride);
+    a.down = bank(down_bank, down_expert_stride);
+    a.x = d_x;
+    a.xrows = d_xrows;
+    a.n_xrows = n_xrows;
+    a.h = d_h;
+    a.out = d_out;
+    a.w = d_w;
+    a.d_model = d_model;
+    a.ff = ff;
+    a.n_used = n_used;
+    a.n_tokens = n_tokens;
+    a.qt_gate = qt_gate;
+    a.qt_up = qt_up;
+    a.qt_down = qt_down;
+    a.accumulate = accumulate;
+    a.err = g_rt.err_d;
+    if (qt_gate == SB_IQ3_S && qt_up == SB_IQ3_S && qt_down == SB_IQ3_S) {
+        const int taken = sb_try_block_iq3s(a, st);
+        if (taken != 0) return taken > 0 ? 0 : -1;
+    }
+    // gather the rows into scratch (grown on demand), then the plain block
+    static float* rows = nullptr;
+    static size_t cap = 0;
+    const size_t need = (size_t)n_tokens * d_model;
+    if (need > cap) {
+        if (rows) {
+            cudaDeviceSynchronize();   // no kernel of an earlier call may still use it
+            cudaFree(rows);
+            rows = nullptr;
+            cap = 0;
+        }
+        if (!sb_cuda_ok(cudaMalloc(&rows, need * sizeof(float)), "block gather scratch")) return -1;
+        cap = need;
+    }
+    if (sb_gather_rows(d_x, n_xrows, d_xrows, n_tokens, d_model, rows, g_rt.err_d, st) != 0) return -1;
+    a.x = rows;
+    a.xrows = nullptr;
+    a.n_xrows = 0;
+    return sb_launch_block(a, st);
+}
+
 // sabah_moe_block_ids over the fixed scratch of the IQ3_S kernels: no device or
 // host memory is allocated, at the price of a size limit and of calls that
 // must not overlap on the GPU (they share that scratch).

@@ -86,10 +86,13 @@ def layer_step(x_own, plan_dev, layer, ops, comm):
     n_tok = x_all.shape[0]
     y = ops.empty_rows(n_tok)
     if P:
-        xp = ops.empty_rows(P)
-        ops.gather(x_all, plan_dev["tok"], xp)
         yp = ops.empty_rows(P)
-        ops.block(layer, xp, plan_dev["lid"], plan_dev["w"], yp)
+        if hasattr(ops, "block_rows"):   # the block reads the pairs' token rows in place
+            ops.block_rows(layer, x_all, plan_dev["tok"], plan_dev["lid"], plan_dev["w"], yp)
+        else:
+            xp = ops.empty_rows(P)
+            ops.gather(x_all, plan_dev["tok"], xp)
+            ops.block(layer, xp, plan_dev["lid"], plan_dev["w"], yp)
         ops.sum_rows(yp, plan_dev["offsets"], y)
     else:
         ops.sum_rows(None, plan_dev["offsets"], y)
@@ -178,6 +181,20 @@ class CudaOps:
                                             ctypes.c_void_p(xp.data_ptr()), ctypes.c_void_p(out.data_ptr()),
                                             ctypes.c_void_p(self._h.data_ptr()), self.d_model, self.ff, 1, P,
                                             self.qt, self.qt, self.qt, 0, self._st()), "sabah_moe_block_ids")
+
+    def block_rows(self, layer, x_all, rows, lid, w, out):
+        """The block on rows `rows` of x_all (one per pair), without a gather pass."""
+        P = out.shape[0]
+        if self._h is None or self._h.shape[0] < P:
+            self._h = self.torch.empty((P, 1, self.ff), dtype=self.torch.float32, device="cuda")
+        g, u, d = self.banks[layer]
+        rt.check(self.L.sabah_moe_block_gather(ctypes.c_void_p(g.data_ptr()), ctypes.c_void_p(u.data_ptr()),
+                                               ctypes.c_void_p(d.data_ptr()), self.gs, self.ds, self.E,
+                                               ctypes.c_void_p(lid.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                               ctypes.c_void_p(x_all.data_ptr()), ctypes.c_void_p(rows.data_ptr()),
+                                               x_all.shape[0], ctypes.c_void_p(out.data_ptr()),
+                                               ctypes.c_void_p(self._h.data_ptr()), self.d_model, self.ff, 1, P,
+                                               self.qt, self.qt, self.qt, 0, self._st()), "sabah_moe_block_gather")
 
     def sum_rows(self, src, offsets, dst):
         n_src = 0 if src is None else src.shape[0]

@@ -101,6 +101,8 @@ SIGNATURES = {
                              c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_vp], c_i),
     "sabah_moe_block_ids_noalloc": ([c_vp, c_vp, c_vp, c_sz, c_sz, c_i, c_vp, c_vp, c_vp, c_vp, c_vp,
                                      c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_vp], c_i),
+    "sabah_moe_block_gather": ([c_vp, c_vp, c_vp, c_sz, c_sz, c_i, c_vp, c_vp, c_vp, c_vp, c_i, c_vp, c_vp,
+                                c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_vp], c_i),
     "sabah_rt_device_error": ([], c_i),
     "sabah_moe_decode": ([c_i, c_vp, c_vp, c_vp, c_sz, c_sz, c_i, c_vp, c_vp, c_vp, c_vp,
                           c_i, c_i, c_i, c_i, c_i, c_i, c_i, c_vp], c_i),

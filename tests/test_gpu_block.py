@@ -166,3 +166,50 @@ def test_block_ids_one_slot_per_token(gpu_rt, orc, T, E):
     ops.moe_block_ids(gate, up, down, ids_d, w_d, x_d, d_model, ff, E, qt, qt, qt, out=acc, accumulate=True)
     torch.cuda.synchronize()
     assert orc.rel_l2(acc.cpu().numpy(), x + got) <= TIGHT
+
+
+@pytest.mark.parametrize("qt,P,E", [(21, 80, 64), (21, 640, 64), (12, 40, 16)])
+def test_block_gather_matches_block_on_gathered_rows(gpu_rt, orc, qt, P, E):
+    """sabah_moe_block_gather (token t reads row xrows[t] of x) equals
+    sabah_moe_block_ids on the gathered rows: in place on the one-launch IQ3_S
+    path (80 pairs), through its gather pass elsewhere (grouped, Q4_K/Q6_K)."""
+    import ctypes
+    from sabah_moe_accelerator_b200 import ops, rt
+    d_model, ff = 2048, 768
+    qd = 14 if qt == 12 else qt
+    n_used = 1 if qt == 21 else 10
+    T = P if qt == 21 else P // n_used
+    gate = ops.synth_rows(E * ff, d_model, qt, seed=81, sigma=0.02)
+    up = ops.synth_rows(E * ff, d_model, qt, seed=82, sigma=0.02)
+    down = ops.synth_rows(E * d_model, ff, qd, seed=83, sigma=0.02)
+    rng = np.random.default_rng(P)
+    n_rows = 37
+    x_all = torch.from_numpy(rng.standard_normal((n_rows, d_model)).astype(np.float32)).cuda()
+    rows = torch.from_numpy(rng.integers(0, n_rows, T).astype(np.int32)).cuda()
+    ids = torch.from_numpy(np.stack([rng.choice(E, n_used, replace=False) for _ in range(T)]).astype(np.int32)).cuda()
+    w = torch.from_numpy((rng.random((T, n_used)) + 0.5).astype(np.float32)).cuda()
+    want = ops.moe_block_ids(gate, up, down, ids, w, x_all[rows.long()].contiguous(), d_model, ff, E, qt, qt, qd)
+    out = torch.empty((T, d_model), device="cuda")
+    h = torch.empty((T, n_used, ff), device="cuda")
+    L = gpu_rt
+    gs, ds = ff * rt.row_bytes(qt, d_model), d_model * rt.row_bytes(qd, ff)
+
+    def call(rws):
+        return L.sabah_moe_block_gather(ctypes.c_void_p(gate.data_ptr()), ctypes.c_void_p(up.data_ptr()),
+                                        ctypes.c_void_p(down.data_ptr()), gs, ds, E, ctypes.c_void_p(ids.data_ptr()),
+                                        ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(x_all.data_ptr()),
+                                        ctypes.c_void_p(rws.data_ptr()), n_rows, ctypes.c_void_p(out.data_ptr()),
+                                        ctypes.c_void_p(h.data_ptr()), d_model, ff, n_used, T, qt, qt, qd, 0,
+                                        ctypes.c_void_p(ops._stream(None)))
+
+    rt.check(call(rows), "sabah_moe_block_gather")
+    torch.cuda.synchronize()
+    assert orc.rel_l2(out.cpu().numpy(), want.cpu().numpy()) <= TIGHT
+    assert L.sabah_rt_device_error() == 0
+    bad = rows.clone()
+    bad[1] = n_rows
+    rt.check(call(bad), "sabah_moe_block_gather, bad row")
+    torch.cuda.synchronize()
+    o = out.cpu().numpy()
+    assert np.isnan(o[1]).all() and np.isfinite(o[0]).all()
+    assert L.sabah_rt_device_error() == 1

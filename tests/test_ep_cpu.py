@@ -118,6 +118,13 @@ class _HostOps:
         x += y
 
 
+class _HostOpsRows(_HostOps):
+    """The same stand-in with the gather folded into the block (ops.block_rows)."""
+
+    def block_rows(self, layer, x_all, rows, lid, w, out):
+        self.block(layer, x_all[rows], lid, w, out)
+
+
 class _GlooComm:
     def __init__(self):
         import torch.distributed as dist
@@ -139,7 +146,7 @@ class _GlooComm:
         return t.numpy()[self.rank * n:(self.rank + 1) * n].copy()
 
 
-def _rank_main(rank, world, port, out_path):
+def _rank_main(rank, world, port, out_path, rows_mode=False):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -155,7 +162,8 @@ def _rank_main(rank, world, port, out_path):
                           "w": pl.w.reshape(-1, 1), "offsets": pl.offsets})
         t0, t1 = ep.token_range(rank, T, world)
         x_own = x0[t0:t1].copy()
-        ep.decode_step(x_own, plans, _HostOps(local), _GlooComm())
+        ops = _HostOpsRows(local) if rows_mode else _HostOps(local)
+        ep.decode_step(x_own, plans, ops, _GlooComm())
         np.save(out_path % rank, x_own)
     finally:
         dist.destroy_process_group()
@@ -167,11 +175,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_gloo_two_ranks_match_single_process_chain(tmp_path, orc):
+@pytest.mark.parametrize("rows_mode", [False, True])
+def test_gloo_two_ranks_match_single_process_chain(tmp_path, orc, rows_mode):
     import torch.multiprocessing as mp
     world = 2
     out = str(tmp_path / "x_%d.npy")
-    mp.start_processes(_rank_main, args=(world, _free_port(), out), nprocs=world, start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, _free_port(), out, rows_mode), nprocs=world, start_method="spawn")
     got = np.concatenate([np.load(out % r) for r in range(world)])
 
     banks, ids, w, x0 = _problem()

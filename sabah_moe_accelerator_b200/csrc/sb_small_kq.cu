@@ -44,7 +44,6 @@
 
 #include "sb_iq3s_core.cuh"   // mbarrier, bulk-copy, PRMT and mma.sync helpers
 
-#define SABAH_API extern "C" __attribute__((visibility("default")))
 
 namespace {
 

@@ -12,9 +12,10 @@
 # once at sabah_rt.cu:1318) is mapped to the Linux member `fd`, which is -1 for
 # every unopened file, so that guarded branch is inert exactly as lanes == 0 is.
 set -euo pipefail
-REF_ROOT="${SABAH_REF_ROOT:-/root/reference}"
-SRC="$REF_ROOT/sabah/runtime/cuda/sabah_rt.cu"
 HERE="$(cd "$(dirname "$0")" && pwd)"
+# the reference project: SABAH_REF_ROOT, else beside this repository
+REF_ROOT="${SABAH_REF_ROOT:-$HERE/../../reference}"
+SRC="$REF_ROOT/sabah/runtime/cuda/sabah_rt.cu"
 OUT="$HERE/_ref"
 if [ ! -f "$SRC" ]; then
     echo "reference source not found: $SRC" >&2

@@ -31,10 +31,11 @@
 //
 // Three kernels share the engine: MUL_MAT_ID (v2 contract), fused gate/up +
 // SwiGLU, and down + top-k weighted combine (+ residual/accumulate).
-// Launches use programmatic dependent launch: a kernel's prologue and weight
-// prefetch overlap the previous kernel; activations and outputs are touched
-// only after griddepcontrol.wait. Every wait is bounded; on timeout the CTA
-// records an error, skips its remaining work and drains its copies.
+// Launches use programmatic dependent launch: a kernel's prologue (barrier
+// set-up, grid-table fill) overlaps the previous kernel; router ids,
+// activations and outputs are touched only after griddepcontrol.wait. Every
+// wait is bounded; on timeout the CTA records an error, skips its remaining
+// work and drains its copies.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -180,6 +181,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
 
     if (warp == kConsumers) {
         // ------------------------------------------------------ producer
+        // The router ids are an input that the previous kernel on the stream
+        // may have written (a router that triggers its dependents early), so
+        // the producer reads them only after that kernel has completed. The
+        // barrier set-up above and the consumers' table fill still overlap it.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         // lane l issues sequence numbers n = l, l + kIssuers, ... (stage n % ns,
         // always the same lane for a given stage); each lane looks up its own
         // tiles' expert addresses, so those loads overlap across lanes
@@ -352,8 +358,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
 }
 
 // ------------------------------------------------------------------ host side
-bool g_attr_set = false;
-int g_num_sms = 0;
+// Per device: the shared-memory attribute is set and the SM count read once
+// with that device current (a process may call on more than one device).
+constexpr int kMaxDevices = 64;
+bool g_attr_set[kMaxDevices] = {};
+int g_num_sms[kMaxDevices] = {};
 
 // split a row of k weights (G = k / 128 groups) over wpt warps, gpw groups each
 bool plan_groups(int k, int& wpt, int& gpw) {
@@ -371,19 +380,25 @@ bool plan_groups(int k, int& wpt, int& gpw) {
 }
 
 int launch(Params& p, cudaStream_t st) {
-    if (!g_attr_set) {
+    int dev = 0;
+    if (!sb_cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return -1;
+    if (dev < 0 || dev >= kMaxDevices) {
+        sb_set_error("the IQ3_S kernels support devices 0..%d", kMaxDevices - 1);
+        return -1;
+    }
+    if (!g_attr_set[dev]) {
         if (!sb_cuda_ok(cudaFuncSetAttribute(k_iq3s, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total),
                         "iq3s smem attribute"))
             return -1;
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        g_attr_set = true;
+        if (!sb_cuda_ok(cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev),
+                        "SM count"))
+            return -1;
+        g_attr_set[dev] = true;
     }
     p.P = kConsumers / p.wpt;
     p.stage_bytes = (16 * p.rb + 127) & ~127;
     p.n_stages = std::min(kMaxStages, (kRingBytes / p.stage_bytes) / kIssuers * kIssuers);
-    const int grid = std::max(1, std::min(p.n_items, g_num_sms));
+    const int grid = std::max(1, std::min(p.n_items, g_num_sms[dev]));
     const int tslot = sb_timing_begin(p.mode == MODE_MMID ? "mmid_iq3s" : p.mode == MODE_GATE_UP ? "gate_up_iq3s"
                                                                                                   : "down_iq3s",
                                       st);
@@ -453,15 +468,13 @@ bool block_scratch(int T, int n_used, int d_model, int ff, cudaStream_t st) {
 }
 
 // Fixed scratch of the allocation-free block (sb_block_iq3s_fixed). Counters
-// occupy the first kFixedCounterBytes whatever the shape; they return to zero
-// after every completed call, so one clearing at set-up (and one after a
-// device error) keeps them valid. The partial sums follow.
+// occupy the first kFixedCounterBytes whatever the shape and are cleared on
+// the call's stream at the start of every call. The partial sums follow.
 constexpr size_t kFixedScratchBytes = (size_t)1 << 20;    // 1 MiB
 constexpr size_t kFixedCounterBytes = (size_t)64 << 10;   // 16,384 counters
-constexpr int kFixedMaxDevices = 64;
+constexpr int kFixedMaxDevices = kMaxDevices;
 struct FixedScratch {
     uint8_t* ptr = nullptr;   // device address of sb_fixed_scratch on this device
-    bool clear = true;        // counters must be zeroed before the next call
 };
 FixedScratch g_fixed[kFixedMaxDevices];
 
@@ -478,10 +491,7 @@ bool fast_path_enabled() {
 
 static __device__ __align__(256) uint8_t sb_fixed_scratch[kFixedScratchBytes];
 
-void sb_block_scratch_invalidate() {
-    g_bs.stale = g_bs.mem != nullptr;
-    for (FixedScratch& f : g_fixed) f.clear = true;
-}
+void sb_block_scratch_invalidate() { g_bs.stale = g_bs.mem != nullptr; }
 
 int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
     if (a.qt != SB_IQ3_S || !fast_path_enabled()) return 0;
@@ -633,12 +643,11 @@ int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st) {
         void* ptr = nullptr;
         if (!sb_cuda_ok(cudaGetSymbolAddress(&ptr, sb_fixed_scratch), "fixed scratch address")) return -1;
         fs.ptr = (uint8_t*)ptr;
-        fs.clear = true;
     }
-    if (fs.clear) {
-        if (!sb_cuda_ok(cudaMemsetAsync(fs.ptr, 0, kFixedCounterBytes, st), "fixed scratch clear")) return -1;
-        fs.clear = false;
-    }
+    // Every call starts from zeroed counters, queued on the call's stream: a
+    // call that gave up part-way (a device error) leaves no stale counts for
+    // the next one. Only this shape's counter words are cleared.
+    if (!sb_cuda_ok(cudaMemsetAsync(fs.ptr, 0, guc + dnc, st), "fixed scratch clear")) return -1;
 
     Params p{};
     p.b = a;

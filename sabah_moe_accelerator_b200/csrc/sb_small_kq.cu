@@ -426,11 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
     }
     __syncthreads();
     // programmatic dependent launch: the next kernel on the stream may start its
-    // prologue (plan, weight copies) as SMs free up. Everything this kernel
-    // reads that an earlier kernel of the block writes (x, h, v), and every
-    // global write, comes after griddepcontrol.wait.
+    // prologue (barrier set-up) as SMs free up. Everything this kernel reads
+    // that an earlier kernel may write (router ids, x, h, v), and every global
+    // write, comes after griddepcontrol.wait.
     asm volatile("griddepcontrol.launch_dependents;");
     if (warp == kW) {
+        // the plan reads the router ids, which the previous kernel on the
+        // stream may have written: wait for it first
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         build_plan(p, smem);
         plan_arrive();
     } else {

@@ -217,3 +217,23 @@ def test_selfcheck_passes_on_product():
         s = r["snapshot"]
         assert s["selfcheck_ok"] == 120 and s["selfcheck_fail"] == 0, s   # 60 per call, two calls
         assert s["selfcheck_max_rel_l2"] < TIGHT, s
+
+
+SENTINEL_DIR = os.path.join(ROOT, "sabah_moe_accelerator_b200", "csrc", "_build")
+
+
+@pytest.mark.parametrize("sentinel,case", [(1, "down"), (1, "gate"), (2, "down"), (3, "down"), (3, "gate")])
+def test_selfcheck_detects_each_sentinel(sentinel, case):
+    """Mutation check, as the reference's tests/test_mul_mat_id_contract.py:120-130:
+    each test-only build plants one routing mistake (1: slot 0 reads the next
+    expert; 2: a slot reads the next slot's input row; 3: a token reads the next
+    token's input). The output must really be wrong, and the runtime's own fp64
+    self-check must say so."""
+    lib = os.path.join(SENTINEL_DIR, "sentinel%d" % sentinel, "libsabah_rt.so")
+    assert os.path.exists(lib), "sentinel build missing (make -C sabah_moe_accelerator_b200/csrc sentinels): " + lib
+    r = _child(case, 21, {"SABAH_LLAMA_SELFCHECK": "60"}, lib=lib)
+    assert r["build_info"].endswith("sentinel=%d" % sentinel), r["build_info"]
+    assert r["rel_vs_exact"] > 50 * TOL, r                     # the output is wrong
+    s = r["snapshot"]
+    assert s["selfcheck_fail"] > 0, s                          # and the in-runtime oracle says so
+    assert s["selfcheck_max_rel_l2"] > 50 * TOL, s

@@ -1,5 +1,7 @@
 """sabah_moe_block_ids_noalloc (fixed device scratch, nothing allocated) against
-sabah_moe_block_ids on the same inputs, both through the C ABI.
+sabah_moe_block_ids on the same inputs, both through the C ABI, and both
+against the float64 oracle of the routed block (reference_block,
+sabah/runtime/executor.py:134-159) over the same dequantized weights.
 
 The file sorts last, so the in-process test runs after every other test has
 used the runtime; the child test runs the same check in a fresh process, where
@@ -29,6 +31,7 @@ def _rel(a, b):
 def check(init: bool) -> None:
     import torch
 
+    from oracle import cpu as orc
     from sabah_moe_accelerator_b200 import ops, rt
     if init:
         ops.init(0)
@@ -39,6 +42,7 @@ def check(init: bool) -> None:
     up = ops.synth_rows(E * ff, d_model, qt, seed=52, sigma=0.02)
     down = ops.synth_rows(E * d_model, ff, qt, seed=53, sigma=0.02)
     gs, ds = ff * rt.row_bytes(qt, d_model), d_model * rt.row_bytes(qt, ff)
+    gh, uh, dh = (t.cpu().numpy().reshape(E, -1) for t in (gate, up, down))
     st = ctypes.c_void_p(ops._stream(None))
     vp = ctypes.c_void_p
 
@@ -60,6 +64,8 @@ def check(init: bool) -> None:
         torch.cuda.synchronize()
         want = out_ref.cpu().numpy()
         assert np.isfinite(want).all()
+        ids_h, w_h, x_h = ids.cpu().numpy(), w.cpu().numpy(), x.cpu().numpy()
+        exact = [orc.moe_block_f64(gh, uh, dh, ids_h[t], w_h[t], x_h[t], d_model, ff, qt, qt, qt) for t in range(T)]
         for call in range(2):   # two calls in a row
             out = torch.full((T, d_model), 7.0, device="cuda")
             h = torch.empty((T, K, ff), device="cuda")
@@ -69,6 +75,8 @@ def check(init: bool) -> None:
             for t in range(T):
                 r = _rel(got[t], want[t])
                 assert r <= TOL and r <= TIGHT, (T, call, t, r)
+                r64 = _rel(got[t].astype(np.float64), exact[t])
+                assert r64 <= TOL, ("vs fp64", T, call, t, r64)
         # accumulate: out += y
         rt.check(run(L.sabah_moe_block_ids_noalloc, T, ids, w, x, out, h, 1), "noalloc accumulate")
         torch.cuda.synchronize()

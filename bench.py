@@ -43,6 +43,12 @@ METRIC = "MoE MUL_MAT_ID tokens/s (IQ3_S decode, 48 x 512-expert bank resident)"
 WORKLOAD = "cfg2: IQ3_S decode, 1 token x 48 blocks, 512 experts/block, top-10, H2048 F768, 49.8 GB bank on 1 GPU"
 
 
+# DRAM bytes (read + write) per decoded block of the persistent decode kernels,
+# from one ncu capture each on the 2-block case (profiles/), keyed by the
+# runtime's kernel-timing name
+DRAM_BYTES_PER_BLOCK = {"decode_iq3s": (40.62e6 + 0.27e6) / 2}
+
+
 def iq3s_row_bytes(k: int) -> int:
     return k // 256 * 110
 
@@ -152,6 +158,62 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def build_cfg2_bank(dev, stream, rank: int = 0, layers: int = LAYERS):
+    """The cfg 2 bank on `dev`: per layer [gate | up | down], 512 experts each,
+    IQ3_S-encoded N(0, 0.02) weights (seed (10 + L) * 4 + role, offset per
+    rank). Returns the one allocation and, per layer, its (gate, up, down) views."""
+    import torch
+    from sabah_moe_accelerator_b200 import ops
+    layer_bytes = EXPERTS * (2 * GU_EXPERT + D_EXPERT)
+    bank = torch.empty(layers * layer_bytes, dtype=torch.uint8, device=dev)
+    views = []
+    with torch.cuda.stream(stream):
+        for Lr in range(layers):
+            base = Lr * layer_bytes
+            trio = []
+            for role, off, rows, k in ((0, 0, FF, D_MODEL), (1, EXPERTS * GU_EXPERT, FF, D_MODEL),
+                                       (2, 2 * EXPERTS * GU_EXPERT, D_MODEL, FF)):
+                view = bank[base + off: base + off + EXPERTS * rows * iq3s_row_bytes(k)]
+                ops.synth_rows(EXPERTS * rows, k, QT_IQ3_S, seed=(10 + Lr) * 4 + role + 7919 * rank, sigma=0.02,
+                               out=view, stream=stream)
+                trio.append(view)
+            views.append(tuple(trio))
+    stream.synchronize()
+    return bank, views
+
+
+def cfg2_parity(views, ids_set, w_set, x_first) -> float:
+    """Decode one token of the benchmark (routing ids_set / w_set [layers][1][K],
+    input x_first [1][d_model]) once through sabah_moe_decode, eagerly, and
+    return its rel-L2 against the fp64 chain of reference_block over the same
+    dequantized weights (the oracle, test infrastructure; outside any timing)."""
+    import torch
+    from oracle import cpu as orc
+    from sabah_moe_accelerator_b200 import ops, rt
+    layers = len(views)
+    dev = views[0][0].device
+    x = torch.from_numpy(np.ascontiguousarray(x_first)).to(dev)
+    h = torch.empty((1, TOP_K, FF), dtype=torch.float32, device=dev)
+    ids_d = torch.from_numpy(np.ascontiguousarray(ids_set)).to(dev)
+    w_d = torch.from_numpy(np.ascontiguousarray(w_set)).to(dev)
+    arr = ctypes.c_void_p * layers
+    G, U, D = (arr(*[v[r].data_ptr() for v in views]) for r in range(3))
+    rt.check(rt.lib().sabah_moe_decode(layers, G, U, D, GU_EXPERT, D_EXPERT, EXPERTS, ids_d.data_ptr(),
+                                       w_d.data_ptr(), x.data_ptr(), h.data_ptr(), D_MODEL, FF, TOP_K, 1,
+                                       QT_IQ3_S, QT_IQ3_S, QT_IQ3_S, ops._stream(None)), "sabah_moe_decode (parity)")
+    torch.cuda.synchronize(dev)
+    got = x.cpu().numpy()[0]
+    want = np.asarray(x_first[0], np.float64)
+    slots = np.arange(TOP_K, dtype=np.int32)
+    for Lr, (g, u, d) in enumerate(views):
+        ids = ids_set[Lr, 0]
+        pick = lambda t, per: np.stack([t[int(i) * per:(int(i) + 1) * per].cpu().numpy() for i in ids])
+        want = want + orc.moe_block_f64(pick(g, GU_EXPERT), pick(u, GU_EXPERT), pick(d, D_EXPERT), slots,
+                                        w_set[Lr, 0], want.astype(np.float32), D_MODEL, FF, QT_IQ3_S, QT_IQ3_S,
+                                        QT_IQ3_S)
+    return float(orc.rel_l2(got, want))
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -164,21 +226,16 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     stream = torch.cuda.Stream(device=dev)
 
     # ---- bank: per layer [gate | up | down], each 512 experts
-    layer_bytes = EXPERTS * (2 * GU_EXPERT + D_EXPERT)
-    bank = torch.empty(LAYERS * layer_bytes, dtype=torch.uint8, device=dev)
-    gate_p, up_p, down_p = [], [], []
-    with torch.cuda.stream(stream):
-        for Lr in range(LAYERS):
-            base = Lr * layer_bytes
-            for role, off, rows, k in ((0, 0, FF, D_MODEL), (1, EXPERTS * GU_EXPERT, FF, D_MODEL),
-                                       (2, 2 * EXPERTS * GU_EXPERT, D_MODEL, FF)):
-                view = bank[base + off: base + off + EXPERTS * rows * iq3s_row_bytes(k)]
-                ops.synth_rows(EXPERTS * rows, k, QT_IQ3_S, seed=(10 + Lr) * 4 + role + 7919 * rank, sigma=0.02,
-                               out=view, stream=stream)
-                (gate_p, up_p, down_p)[role].append(view.data_ptr())
-    stream.synchronize()
+    bank, views = build_cfg2_bank(dev, stream, rank, LAYERS)
+    gate_p, up_p, down_p = ([v[r].data_ptr() for v in views] for r in range(3))
 
     ids_np, w_np = routing(ROUTING_SETS, LAYERS)
+    # parity of the timed shape before timing it: routing set 0, all layers, fp64 chain
+    parity = None
+    if not args.no_parity:
+        parity = cfg2_parity(views, ids_np[0], w_np[0], x0())
+        if not parity <= 2e-3:
+            raise SystemExit("cfg2 parity failed: rel-L2 %.3e against the fp64 chain" % parity)
     ids_d = torch.from_numpy(ids_np).to(dev)
     w_d = torch.from_numpy(w_np).to(dev)
     x0_d = torch.from_numpy(x0()).to(dev)
@@ -254,11 +311,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     gu_bytes = TOP_K * 2 * FF * GU_ROW + D_MODEL * 4 + TOP_K * FF * 4
     dn_bytes = TOP_K * D_MODEL * D_ROW + TOP_K * FF * 4 + 2 * D_MODEL * 4
     kbytes = {"gate_up": gu_bytes, "down": dn_bytes, "decode": LAYERS * (gu_bytes + dn_bytes)}
-    # DRAM bytes per launch from one ncu capture of k_decode_iq3s on the 2-block
-    # case (40.62 MB read + 0.27 MB written), scaled to the blocks decoded
-    traffic = {"decode": int(round((40.62e6 + 0.27e6) / 2 * LAYERS))}
     dom_name, dom = max(ktimes.items(), key=lambda kv: kv[1][1])
     family = "decode" if "decode" in dom_name else "gate_up" if "gate_up" in dom_name else "down"
+    # DRAM bytes per launch: the ncu capture of the dominant kernel on the
+    # 2-block case (profiles/), per block, scaled to the blocks decoded
+    per_block = DRAM_BYTES_PER_BLOCK.get(dom_name)
+    traffic = {"decode": int(round(per_block * LAYERS))} if per_block else {}
     avg_ms = dom[1] / dom[0]
     peaks, peak_kind = measured_peaks()
     achieved = kbytes[family] / (avg_ms * 1e-3) / 1e9
@@ -323,6 +381,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "path": "sabah_moe_decode (C ABI), eager launches"},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clk,
+        "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3, "checked": "routing set 0, all %d blocks, before timing"
+                   % LAYERS} if parity is not None else None,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(bank, gate_p, up_p, down_p, ids_np, w_np, use_ref=False)
@@ -1049,6 +1109,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the fp64 check of the timed shape that runs before timing (profiling only)")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5", "cfg5s"],
                     help="cfg2: the headline 1-token decode (replicas for N > 1); cfg3: 512-token prefill "
                          "of one block; cfg4: Q4_K/Q6_K batch-4 decode; cfg5: expert-parallel bank; cfg5s: "

@@ -572,10 +572,17 @@ bool fast_path_enabled() {
 
 }  // namespace
 
-void sb_decode_scratch_invalidate() { g_ds.stale = g_ds.mem != nullptr; }
+void sb_decode_scratch_invalidate() {
+    g_ds.stale = g_ds.mem != nullptr;
+    sb_flow_scratch_invalidate();
+}
 
 int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !fast_path_enabled()) return 0;
+    // one token: the barrier-free kernel (sb_flow_iq3s.cu); more tokens, gathered
+    // rows or shapes it does not cover: the phase-barrier kernel below
+    const int flow = sb_try_flow_iq3s(a, st);
+    if (flow != 0) return flow;
     if (a.n_layers < 1 || a.n_layers > kMaxLayers || a.n_tokens < 1 || a.n_used < 1 || a.n_used > kMaxUsed) return 0;
     DecodeParams p{};
     if (!plan(a.d_model, a.ff, 1, p.gu) || !plan(a.ff, a.d_model, 2, p.dn)) return 0;

@@ -1,0 +1,714 @@
+// Barrier-free persistent IQ3_S decode for one token: every layer of a decode
+// step (sabah_moe_decode), or one block (sabah_moe_block_ids with one token),
+// in ONE cooperative launch, one CTA per SM.
+//
+// The per-layer dependency chain x_L -> h_L -> x_{L+1} is all-to-all: every
+// gate/up row needs all of x_L, every down row all of h_L. The kernel of
+// sb_decode_iq3s.cu meets it with a grid barrier per phase and a rebuild of
+// the phase's input in every CTA afterwards (two L2 round trips per phase).
+// Here the data carries its own readiness instead:
+//
+// * x and h live in global memory as 64-bit (value, tag) pairs, written with
+//   one relaxed store each. A pair is single-copy atomic, so a reader that sees
+//   the tag of layer L also sees that layer's value: one round trip, no flag,
+//   no barrier. Tags are (epoch << 6) + L + 1; the epoch word is bumped by the
+//   last CTA to exit, so a CUDA-graph replay never mistakes an earlier
+//   launch's pairs for its own. x and h are double-buffered by layer parity.
+// * Work is balanced on the warp: a gate/up item is 8 gate rows and the same 8
+//   up rows of one slot (a stacked 16-row MMA tile) over the full row; items go
+//   round-robin over the CTAs (n_used * ff / 8 = 960 items on 148 CTAs), and
+//   consumer warp w takes group w (128 weights) of every item, so each warp does
+//   exactly the CTA's item count of groups. The item's last warp sums the 16
+//   warps' partial rows in fixed order and publishes h = silu(g) * u.
+//   Round-robin order finishes slot 0 first, so down work can start on it
+//   while later slots are still in flight.
+// * A down unit is 16 output rows over all n_used slots (d_model / 16 = 128
+//   units, one per CTA); its tasks (slot, group) go round-robin over the
+//   warps. A task needs only its own 128 values of h: the warp polls those
+//   pairs, converts them to the B fragments of mma.sync in registers, and runs.
+//   The unit's last task sums the partial rows (groups in order, then slots in
+//   order, weighted) and publishes x_{L+1} = x_L + y.
+// * In gate/up, warp w's B fragments (group w of x) are built once per layer
+//   and kept in registers for all its items.
+// * Weights are inputs, so the producer warp streams tiles of the next items
+//   (next layers included) while consumers wait for data.
+//
+// The decode core (grid lookup + PRMT into fp16 subnormals + mma.sync with x
+// in fp16 hi/lo parts, scale per sub-block) is the one of sb_iq3s_core.cuh.
+//
+// Every wait is bounded (stage barriers, sequence stamps, pair polls). A CTA
+// that gives up records SB_DERR_TIMEOUT, raises a global abort word that the
+// other CTAs' polls read, skips its remaining work and drains its copies.
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+
+#include "sb_iq3s_core.cuh"
+
+namespace {
+
+using namespace sb_iq3s;
+
+constexpr int kNC = 16;                      // consumer warps
+constexpr int kThreads = (kNC + 1) * 32;     // + one producer warp
+constexpr int kLogR = 5;                     // 32 grid-table replicas: conflict-free lookups
+constexpr int kR = 1 << kLogR;
+constexpr int kStageBytes = 16 * 880;        // a stacked gate/up tile at d_model <= 2048
+constexpr int kStages = 9;                   // = issuing producer lanes: lane l owns stage l
+constexpr int kMaxLayers = 64;               // tags hold the layer in 6 bits
+constexpr int kMaxUsed = 16;
+constexpr int kMaxDnTasks = 160;             // n_used * ff / 128
+constexpr long long kPollLimit = 1ll << 21;  // pair polls (~1 us each)
+
+struct Desc {
+    int seq;    // sequence number of the stage's current contents
+    int bad;    // bit t: tile t of the stage has an id outside [0, n_experts)
+    int a, b;   // gate/up: slot, 8-row block; down: first slot, tiles
+};
+
+struct Smem {
+    static constexpr int table = 0;
+    static constexpr int stages = table + table_bytes<kR>();
+    static constexpr int red = stages + kStages * kStageBytes;          // [kStages][kNC][16] float
+    static constexpr int dred = red + kStages * kNC * 16 * 4;          // [kMaxDnTasks][16] float
+    static constexpr int bst = dred + kMaxDnTasks * 16 * 4;            // [kNC][32][16 B] B staging
+    static constexpr int xown = bst + kNC * 512;                       // [16] float: the unit's x rows
+    static constexpr int desc = xown + 16 * 4;                         // [kStages] Desc
+    static constexpr int cnt = desc + kStages * (int)sizeof(Desc);     // [kStages] int
+    static constexpr int ucnt = cnt + kStages * 4;                     // int: finished down tasks
+    static constexpr int abort_flag = ucnt + 4;
+    static constexpr int bars = (abort_flag + 4 + 7) & ~7;             // full[kStages], empty[kStages]
+    static constexpr int total = bars + 2 * kStages * 8;
+};
+static_assert(Smem::total <= 227 * 1024, "shared memory budget");
+static_assert(Smem::stages % 128 == 0 && kStageBytes % 128 == 0, "stage alignment");
+static_assert(Smem::bst % 16 == 0, "B staging alignment");
+
+struct FlowLayer {
+    const uint8_t* gate;
+    const uint8_t* up;
+    const uint8_t* down;
+    const int32_t* ids;   // [n_used]
+    const float* w;       // [n_used]
+};
+
+struct FlowParams {
+    int n_layers, n_used, n_experts, d_model, ff;
+    int rb_gu, rb_dn;          // row bytes
+    int G, Gd;                 // 128-weight groups per gate/up row and per down row
+    int n_gu_items;            // n_used * ff / 8
+    int n_units;               // d_model / 16
+    int tps;                   // down tiles per stage (1 or 2)
+    int n_dn_stages;           // ceil(n_used / tps)
+    size_t gu_stride, dn_stride;
+    const float* x;            // the input of block 0
+    float* out;                // the last block's destination: (accumulate ? out : 0) + y
+    int accumulate;
+    float* h;                  // [n_used][ff]: h of the last block
+    unsigned long long* xpairs;   // [2][d_model]
+    unsigned long long* hpairs;   // [2][n_used][ff]
+    unsigned* ctl;             // [0] epoch, [1] CTAs exited, [2] global abort
+    int* err;
+    FlowLayer layer[kMaxLayers];
+};
+
+__device__ inline void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNC * 32) : "memory"); }
+
+__device__ inline unsigned ld_relaxed_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ inline void st_relaxed_u32(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ inline void st_pair(unsigned long long* p, float v, unsigned tag) {
+    const unsigned long long u = ((unsigned long long)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(u) : "memory");
+}
+
+// This CTA gives up: local and global abort flags, and the error word.
+__device__ inline void give_up(volatile int* abort_flag, unsigned* gabort, int* err) {
+    *abort_flag = 1;
+    st_relaxed_u32(gabort, 1u);
+    if (err) atomicExch(err, SB_DERR_TIMEOUT);
+}
+__device__ inline bool aborting(volatile int* abort_flag, const unsigned* gabort) {
+    return *abort_flag || ld_relaxed_u32(gabort);
+}
+// Warp-uniform forms: every lane of the warp gets the same answer, so the
+// warp never splits before a shuffle, a vote or mma.sync.
+__device__ inline bool warp_aborting(volatile int* abort_flag, const unsigned* gabort) {
+    return __any_sync(0xffffffffu, aborting(abort_flag, gabort));
+}
+__device__ inline bool warp_wait_stage(const int* stamp, int seq, uint32_t full, uint32_t parity, int* err,
+                                       volatile int* abort_flag) {
+    const bool stamped = __all_sync(0xffffffffu, wait_seq(stamp, seq, err, abort_flag));
+    return stamped && __all_sync(0xffffffffu, mbar_wait(full, parity, err, abort_flag));
+}
+
+// Warp-cooperative: lane l reads pairs [4l, 4l + 4) at p and returns their
+// values once all 32 lanes see `tag` on all four. False if the kernel is
+// aborting or the wait gives up.
+__device__ inline bool poll4(const unsigned long long* p, unsigned tag, float4& out, volatile int* abort_flag,
+                             unsigned* gabort, int* err) {
+    const unsigned long long* q = p + 4 * (threadIdx.x & 31);
+    for (long long i = 0; i < kPollLimit; ++i) {
+        unsigned long long v0, v1, v2, v3;
+        asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "l"(q) : "memory");
+        asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v2), "=l"(v3) : "l"(q + 2) : "memory");
+        const bool ok = (unsigned)(v0 >> 32) == tag && (unsigned)(v1 >> 32) == tag && (unsigned)(v2 >> 32) == tag &&
+                        (unsigned)(v3 >> 32) == tag;
+        if (__all_sync(0xffffffffu, ok)) {
+            out = make_float4(__uint_as_float((unsigned)v0), __uint_as_float((unsigned)v1),
+                              __uint_as_float((unsigned)v2), __uint_as_float((unsigned)v3));
+            return true;
+        }
+        if ((i & 7) == 7 && __any_sync(0xffffffffu, aborting(abort_flag, gabort))) return false;
+        __nanosleep(64);
+    }
+    if ((threadIdx.x & 31) == 0) give_up(abort_flag, gabort, err);
+    return false;
+}
+
+// B fragments of mma.sync m16n8k16 for one 128-element group of a vector, lane
+// l holding elements [4l, 4l + 4): per sub-block (8 lanes) a power-of-two
+// scale puts the max into [2^13, 2^14); each value splits into fp16 hi and lo.
+// Lane (g, c) gets, for step S, the hi (g even) or lo (g odd) pairs of entry S
+// of sub-block c when g / 2 == c, zeros otherwise (the K permutation of the
+// decode core), and inv = 2^24 / scale of sub-block c.
+__device__ inline void build_b(float4 v4, uint32_t bst, uint32_t (&bf)[8][2], float& inv) {
+    const int lane = threadIdx.x & 31;
+    float m = fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    int ex = 0;
+    if (m > 0.f && isfinite(m)) {
+        frexpf(m, &ex);   // m = f * 2^ex, f in [0.5, 1)
+        ex = max(-100, min(100, 14 - ex));
+    }
+    const float s = ldexpf(1.f, ex);
+    const float v[4] = {v4.x * s, v4.y * s, v4.z * s, v4.w * s};
+    __half hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        hi[i] = __float2half_rn(v[i]);
+        lo[i] = __float2half_rn(v[i] - __half2float(hi[i]));
+    }
+    const __half2 h01 = __halves2half2(hi[0], hi[1]), h23 = __halves2half2(hi[2], hi[3]);
+    const __half2 l01 = __halves2half2(lo[0], lo[1]), l23 = __halves2half2(lo[2], lo[3]);
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(bst + 16u * lane), "r"(*(const uint32_t*)&h01),
+                 "r"(*(const uint32_t*)&h23), "r"(*(const uint32_t*)&l01), "r"(*(const uint32_t*)&l23)
+                 : "memory");
+    const float my_inv = 16777216.0f / s;   // 2^24 undoes the subnormal encoding of the weights
+    __syncwarp();
+    const int g = lane >> 2, c = lane & 3;
+    inv = __shfl_sync(0xffffffffu, my_inv, 8 * c);
+    const bool mine = (g >> 1) == c;
+    const uint32_t src = bst + 16u * (8 * c) + 8u * (g & 1);
+#pragma unroll
+    for (int S = 0; S < 8; ++S) {
+        uint32_t b0 = 0, b1 = 0;
+        if (mine) asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(src + 16u * S));
+        bf[S][0] = b0;
+        bf[S][1] = b1;
+    }
+    __syncwarp();   // the staging area may be rewritten after this
+}
+
+// Fields of rows g (h = 0) and g + 8 (h = 1) for sub-block 4N + c of the
+// super-block at shared address sb (row 0): 8 qs bytes (4 u16), 4 sign
+// bytes, the qh byte spread to one 0/1 byte per entry, and the scale
+// db = d * (1 + 2 * nibble) * inv.
+template <int N>
+__device__ inline void fields(uint32_t sb, const Lane& L, float inv, uint32_t (&qsw)[2][4], uint32_t (&QH)[2][2],
+                              uint32_t (&sgw)[2][4], float (&db)[2]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t r8 = sb + L.row8c + h * L.rb8, r4 = sb + L.row4c + h * L.rb8;
+        const uint32_t r1 = sb + L.row1c + h * L.rb8, rh = sb + L.rowhc + h * L.rb8;
+        const float d = __half2float(__ushort_as_half((unsigned short)ld_u16<0>(sb + L.row0 + h * L.rb8)));
+        qsw[h][0] = ld_u16<2 + 32 * N>(r8);
+        qsw[h][1] = ld_u16<4 + 32 * N>(r8);
+        qsw[h][2] = ld_u16<6 + 32 * N>(r8);
+        qsw[h][3] = ld_u16<8 + 32 * N>(r8);
+        sgw[h][0] = ld_u8<74 + 16 * N>(r4);
+        sgw[h][1] = ld_u8<75 + 16 * N>(r4);
+        sgw[h][2] = ld_u8<76 + 16 * N>(r4);
+        sgw[h][3] = ld_u8<77 + 16 * N>(r4);
+        const uint32_t qh = ld_u8<66 + 4 * N>(r1);
+        QH[h][0] = ((qh & 15u) * 0x00204081u) & 0x01010101u;   // qh bits 0..3 -> bytes 0..3
+        QH[h][1] = ((qh >> 4) * 0x00204081u) & 0x01010101u;    // qh bits 4..7 -> bytes 0..3
+        const uint32_t nib = (ld_u8<106 + 2 * N>(rh) >> L.nib_shift) & 15u;
+        db[h] = d * (float)(1 + 2 * (int)nib) * inv;
+    }
+}
+
+// Step S (grid entry S of the lane's sub-block) for rows g and g + 8: decode
+// into A fragments and issue the MMA into accumulator S & 1.
+template <int S>
+__device__ inline void step1(uint32_t table, const uint32_t (&qsw)[2][4], const uint32_t (&QH)[2][2],
+                             const uint32_t (&sgw)[2][4], const uint32_t (&bf)[8][2], float (&dd)[2][4]) {
+    // PRMT selector: byte 0 = qs byte (S & 1) of the u16 word, byte 1 = QH byte (S & 3), bytes 2, 3 = 0
+    constexpr uint32_t sel = (uint32_t)(S & 1) | ((4u + (S & 3)) << 4) | (2u << 8) | (2u << 12);
+    constexpr uint32_t mask = (S & 1) ? 0xF0u : 0x0Fu;                 // entry S's sign nibble
+    constexpr uint32_t kspread = (S & 1) ? 0x01020408u : 0x10204080u;  // nibble bits -> bit 7 of bytes 0..3
+    uint32_t a[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t idx = prmt(qsw[h][S >> 1], QH[h][S >> 2], sel);
+        uint32_t grid;
+        asm("ld.shared.u32 %0, [%1];" : "=r"(grid) : "r"((idx << (kLogR + 2)) + table));
+        const uint32_t Z = ((sgw[h][S >> 1] & mask) * kspread) & 0x80808080u;
+        a[h][0] = prmt(grid, Z, 0x5140);   // (e0, e1) as signed fp16 subnormals
+        a[h][1] = prmt(grid, Z, 0x7362);   // (e2, e3)
+    }
+    mma16816(dd[S & 1], a[0][0], a[1][0], a[0][1], a[1][1], bf[S][0], bf[S][1]);
+}
+
+// One 128-weight group (sub-blocks 4N .. 4N + 3 of the super-block at sb) of a
+// 16-row tile: adds the dots of rows g and g + 8 (this lane's sub-block) to acc.
+template <int N>
+__device__ inline void do_group(uint32_t sb, const Lane& L, const uint32_t (&bf)[8][2], float inv, float (&acc)[2]) {
+    uint32_t qsw[2][4], QH[2][2], sgw[2][4];
+    float db[2];
+    fields<N>(sb, L, inv, qsw, QH, sgw, db);
+    float dd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    step1<0>(L.table, qsw, QH, sgw, bf, dd);
+    step1<1>(L.table, qsw, QH, sgw, bf, dd);
+    step1<2>(L.table, qsw, QH, sgw, bf, dd);
+    step1<3>(L.table, qsw, QH, sgw, bf, dd);
+    step1<4>(L.table, qsw, QH, sgw, bf, dd);
+    step1<5>(L.table, qsw, QH, sgw, bf, dd);
+    step1<6>(L.table, qsw, QH, sgw, bf, dd);
+    step1<7>(L.table, qsw, QH, sgw, bf, dd);
+    acc[0] = fmaf(db[0], (dd[0][0] + dd[0][1]) + (dd[1][0] + dd[1][1]), acc[0]);
+    acc[1] = fmaf(db[1], (dd[0][2] + dd[0][3]) + (dd[1][2] + dd[1][3]), acc[1]);
+}
+
+// group q of a row: super-block q / 2, half q % 2
+__device__ inline void do_group_q(uint32_t tile, int q, const Lane& L, const uint32_t (&bf)[8][2], float inv,
+                                  float (&acc)[2]) {
+    const uint32_t sb = tile + (uint32_t)(q >> 1) * 110u;
+    if (q & 1)
+        do_group<1>(sb, L, bf, inv, acc);
+    else
+        do_group<0>(sb, L, bf, inv, acc);
+}
+
+// rows g, g + 8 of the quad's partial sums, summed over the quad (c = 0..3)
+__device__ inline void quad_sum(float (&acc)[2]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
+        acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
+    }
+}
+
+// Gate/up items go round-robin over the CTAs in reverse order (item i to CTA
+// grid - 1 - i % grid), so the CTAs that get one item more than the rest
+// include those without a down unit (the units take CTAs 0 .. n_units - 1).
+__device__ inline int gu_rank(int cta) { return (int)gridDim.x - 1 - cta; }
+__device__ inline int gu_items_of(const FlowParams& p, int cta) {
+    const int r = gu_rank(cta);
+    return r < p.n_gu_items ? (p.n_gu_items - 1 - r) / (int)gridDim.x + 1 : 0;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant__ FlowParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+    uint64_t* bars = (uint64_t*)(smem + Smem::bars);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages);
+    volatile int* abort_flag = (volatile int*)(smem + Smem::abort_flag);
+    Desc* descs = (Desc*)(smem + Smem::desc);
+    unsigned* gabort = p.ctl + 2;
+
+    const int ng = gu_items_of(p, cta);                        // gate/up items of this CTA per layer
+    const int nd = cta < p.n_units ? p.n_dn_stages : 0;       // down stages of this CTA per layer
+    const int per = ng + nd;
+
+    if (threadIdx.x == 0) {
+        *abort_flag = 0;
+        *(int*)(smem + Smem::ucnt) = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);   // one release per use, by the stage's last user
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < kStages) {
+        ((int*)(smem + Smem::cnt))[threadIdx.x] = 0;
+        descs[threadIdx.x].seq = -1;
+    }
+    __syncthreads();
+
+    if (warp == kNC) {
+        // ------------------------------------------------------------ producer
+        // lane l issues this CTA's sequence numbers n = l, l + kStages, ...
+        // over all layers, always into stage l
+        if (lane < kStages) {
+            const uint32_t st0 = smem_u32(smem + Smem::stages);
+            const int total = p.n_layers * per;
+            int last = -1;
+            for (int n = lane; n < total; n += kStages) {
+                if (aborting(abort_flag, gabort)) break;
+                const int s = n % kStages;
+                if (n >= kStages && !mbar_wait(empty0 + 8 * s, ((n / kStages) - 1) & 1, p.err, abort_flag)) break;
+                const int L = n / per, idx = n % per;
+                const FlowLayer& lb = p.layer[L];
+                Desc d;
+                d.bad = 0;
+                const uint8_t* src[2] = {nullptr, nullptr};
+                uint32_t bytes[2] = {0, 0}, off[2] = {0, 0};
+                int nt;
+                if (idx < ng) {
+                    // stacked gate/up tile: 8 gate rows, then the same 8 up rows
+                    const int item = gu_rank(cta) + idx * (int)gridDim.x;
+                    const int rpb = p.ff / 8;
+                    d.a = item / rpb;
+                    d.b = item % rpb;
+                    int id = lb.ids[d.a];
+#if SABAH_SENTINEL == 1
+                    if (d.a == 0 && id >= 0 && id < p.n_experts) id = (id + 1) % p.n_experts;   // test-only build
+#endif
+                    nt = 2;
+                    if (id < 0 || id >= p.n_experts) {
+                        d.bad = 1;
+                    } else {
+                        const size_t o = (size_t)id * p.gu_stride + (size_t)d.b * 8 * p.rb_gu;
+                        src[0] = lb.gate + o;
+                        src[1] = lb.up + o;
+                        bytes[0] = bytes[1] = 8u * p.rb_gu;
+                        off[1] = 8u * p.rb_gu;
+                    }
+                } else {
+                    // down tiles: 16 rows of this CTA's unit for tps consecutive slots
+                    const int ds = idx - ng;
+                    d.a = ds * p.tps;
+                    d.b = min(p.tps, p.n_used - d.a);
+                    nt = d.b;
+                    for (int t = 0; t < nt; ++t) {
+                        int id = lb.ids[d.a + t];
+#if SABAH_SENTINEL == 1
+                        if (d.a + t == 0 && id >= 0 && id < p.n_experts) id = (id + 1) % p.n_experts;
+#endif
+                        if (id < 0 || id >= p.n_experts) {
+                            d.bad |= 1 << t;
+                        } else {
+                            src[t] = lb.down + (size_t)id * p.dn_stride + (size_t)cta * 16 * p.rb_dn;
+                            bytes[t] = 16u * p.rb_dn;
+                            off[t] = (uint32_t)t * 16u * p.rb_dn;
+                        }
+                    }
+                }
+                d.seq = -1;
+                descs[s] = d;
+                __threadfence_block();
+                *(volatile int*)&descs[s].seq = n;   // the stage's previous use is released
+                uint32_t tot = 0;
+                for (int t = 0; t < nt; ++t) tot += bytes[t];
+                if (tot) {
+                    mbar_expect_tx(full0 + 8 * s, tot);
+                    for (int t = 0; t < nt; ++t)
+                        if (bytes[t]) bulk_g2s(st0 + s * kStageBytes + off[t], src[t], bytes[t], full0 + 8 * s);
+                } else {
+                    mbar_arrive(full0 + 8 * s);
+                }
+                last = n;
+            }
+            // never leave with a copy in flight: the last use of this lane's stage must have landed
+            if (last >= 0)
+                for (long long i = 0; i < kSpinLimit && !mbar_try_wait(full0 + 8 * (last % kStages),
+                                                                       (last / kStages) & 1); ++i) {
+                }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------- consumers
+    uint32_t* table = (uint32_t*)(smem + Smem::table);
+    fill_table<kNC * 32, kR>(table);
+    consumers_sync();
+    const int g = lane >> 2, c = lane & 3;
+    const Lane Lg = lane_init<kR>(table, p.rb_gu, lane);
+    const Lane Ld = lane_init<kR>(table, p.rb_dn, lane);
+    const uint32_t stages32 = smem_u32(smem + Smem::stages);
+    const uint32_t bst = smem_u32(smem + Smem::bst) + 512u * warp;
+    float* red = (float*)(smem + Smem::red);
+    float* dred = (float*)(smem + Smem::dred);
+    float* xown = (float*)(smem + Smem::xown);
+    int* cnt = (int*)(smem + Smem::cnt);
+    int* ucnt = (int*)(smem + Smem::ucnt);
+    const unsigned epoch = ld_relaxed_u32(p.ctl);
+    const int n_tasks = p.n_used * p.Gd;
+    const float nan = __int_as_float(0x7fc00000);
+
+    for (int L = 0; L < p.n_layers; ++L) {
+        const unsigned tag = (epoch << 6) + (unsigned)L + 1u;
+        const FlowLayer& lb = p.layer[L];
+        const int seq0 = L * per;
+        // ------------------------------------------------ gate/up: group `warp` of every item
+        if (warp < p.G && ng > 0) {
+            uint32_t bf[8][2];
+            float inv = 0.f;
+            float4 xv;
+            bool have;
+            if (L == 0) {
+                xv = __ldcg((const float4*)(p.x + 128 * warp) + lane);
+                have = !warp_aborting(abort_flag, gabort);
+            } else {
+                have = poll4(p.xpairs + (size_t)(L & 1) * p.d_model + 128 * warp, tag, xv, abort_flag, gabort, p.err);
+            }
+            if (have) build_b(xv, bst, bf, inv);
+            for (int k = 0; k < ng && have; ++k) {
+                const int n = seq0 + k, s = n % kStages;
+                if (!warp_wait_stage(&descs[s].seq, n, full0 + 8 * s, (n / kStages) & 1, p.err, abort_flag)) {
+                    have = false;
+                    break;
+                }
+                const Desc d = descs[s];
+                float acc[2] = {0.f, 0.f};
+                if (!d.bad) do_group_q(stages32 + s * kStageBytes, warp, Lg, bf, inv, acc);
+                quad_sum(acc);
+                float* rr = red + (s * kNC + warp) * 16;
+                if (c == 0) {
+                    rr[g] = acc[0];
+                    rr[g + 8] = acc[1];
+                }
+                __threadfence_block();
+                __syncwarp();
+                int lastw = 0;
+                if (lane == 0) lastw = atomicAdd(cnt + s, 1) == p.G - 1;
+                lastw = __shfl_sync(0xffffffffu, lastw, 0);
+                if (!lastw) continue;
+                // ---- the item's last warp: rows in fixed warp order, then h = silu(g) * u
+                __threadfence_block();
+                float v = 0.f;
+                if (lane < 16)
+                    for (int w = 0; w < p.G; ++w) v += red[(s * kNC + w) * 16 + lane];
+                const float u = __shfl_sync(0xffffffffu, v, (lane + 8) & 31);
+                __syncwarp();
+                if (lane == 0) {
+                    cnt[s] = 0;
+                    __threadfence_block();
+                    mbar_arrive(empty0 + 8 * s);   // the tile and its partial rows are consumed
+                    if (d.bad && p.err) atomicExch(p.err, SB_DERR_BAD_ID);
+                }
+                if (lane < 8) {
+                    const float hv = d.bad ? nan : v / (1.f + expf(-v)) * u;
+                    const size_t row = (size_t)d.a * p.ff + (size_t)d.b * 8 + lane;
+                    st_pair(p.hpairs + (size_t)(L & 1) * p.n_used * p.ff + row, hv, tag);
+                    p.h[row] = hv;
+                }
+            }
+        }
+        // ------------------------------------------------ down: tasks (slot, group) of this CTA's unit
+        if (nd > 0) {
+            const int unit = cta;
+            for (int t = warp; t < n_tasks; t += kNC) {
+                if (warp_aborting(abort_flag, gabort)) break;
+                const int e = t / p.Gd, j = t % p.Gd;
+                const int ds = e / p.tps, n = seq0 + ng + ds, s = n % kStages;
+                float4 hv;
+                if (!poll4(p.hpairs + (size_t)(L & 1) * p.n_used * p.ff + (size_t)e * p.ff + 128 * j, tag, hv,
+                           abort_flag, gabort, p.err))
+                    break;
+                uint32_t bf[8][2];
+                float inv;
+                build_b(hv, bst, bf, inv);
+                if (!warp_wait_stage(&descs[s].seq, n, full0 + 8 * s, (n / kStages) & 1, p.err, abort_flag)) break;
+                const Desc d = descs[s];
+                const int tl = e - d.a;
+                const bool bad = (d.bad >> tl) & 1;
+                float acc[2] = {0.f, 0.f};
+                if (!bad)
+                    do_group_q(stages32 + s * kStageBytes + (uint32_t)tl * 16u * p.rb_dn, j, Ld, bf, inv, acc);
+                quad_sum(acc);
+                if (c == 0) {
+                    dred[t * 16 + g] = bad ? nan : acc[0];
+                    dred[t * 16 + g + 8] = bad ? nan : acc[1];
+                }
+                __threadfence_block();
+                __syncwarp();
+                int ulast = 0;
+                if (lane == 0) {
+                    // release the stage once all its tasks are done
+                    const int in_stage = d.b * p.Gd;
+                    if (atomicAdd(cnt + s, 1) == in_stage - 1) {
+                        cnt[s] = 0;
+                        __threadfence_block();
+                        mbar_arrive(empty0 + 8 * s);
+                    }
+                    if (bad && p.err) atomicExch(p.err, SB_DERR_BAD_ID);
+                    ulast = atomicAdd(ucnt, 1) == n_tasks - 1;
+                }
+                ulast = __shfl_sync(0xffffffffu, ulast, 0);
+                if (!ulast) continue;
+                // ---- the unit's last task: groups in order, slots in order (weighted), residual
+                __threadfence_block();
+                const int r = lane & 15;
+                const int row = unit * 16 + r;
+                float tot = 0.f;
+                for (int e2 = 0; e2 < p.n_used; ++e2) {
+                    float v = 0.f;
+                    for (int j2 = 0; j2 < p.Gd; ++j2) v += dred[(e2 * p.Gd + j2) * 16 + r];
+                    tot += __ldg(lb.w + e2) * v;
+                }
+                float base;
+                if (L == 0)
+                    base = p.accumulate ? p.out[row] : 0.f;
+                else
+                    base = xown[r];
+                const float nv = base + tot;
+                __syncwarp();
+                if (lane < 16) {
+                    xown[r] = nv;   // next layer's base (read by this CTA's combine only)
+                    if (L + 1 < p.n_layers)
+                        st_pair(p.xpairs + (size_t)((L + 1) & 1) * p.d_model + row, nv, tag + 1u);
+                    else
+                        p.out[row] = nv;
+                }
+                __threadfence_block();
+                __syncwarp();
+                if (lane == 0) atomicExch(ucnt, 0);
+            }
+        }
+    }
+
+    // a CTA whose own wait gave up tells the others (their polls read the word)
+    if (*abort_flag && lane == 0) st_relaxed_u32(gabort, 1u);
+    // the last CTA out advances the epoch and clears the exit count and the abort word
+    consumers_sync();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(p.ctl + 1, 1u) == gridDim.x - 1) {
+            p.ctl[1] = 0;
+            p.ctl[2] = 0;
+            p.ctl[0] = p.ctl[0] + 1u;
+            __threadfence();
+        }
+    }
+}
+
+// ------------------------------------------------------------------ host side
+struct FlowScratch {
+    void* mem = nullptr;
+    bool stale = false;
+};
+FlowScratch g_fs;
+constexpr size_t kCtlBytes = 256;
+constexpr size_t kXPairBytes = 2 * 2048 * 8;
+constexpr size_t kHPairBytes = 2 * (size_t)kMaxUsed * 2048 * 8;
+constexpr int kMaxDev = 64;
+bool g_flow_attr[kMaxDev] = {};
+int g_flow_grid[kMaxDev] = {};
+
+bool flow_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* v = std::getenv("SABAH_IQ3S_FLOW");
+        on = !(v && *v == '0');
+    }
+    return on != 0;
+}
+
+bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+void sb_flow_scratch_invalidate() { g_fs.stale = g_fs.mem != nullptr; }
+
+int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
+    if (!flow_enabled()) return 0;
+    if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S) return 0;
+    if (a.n_tokens != 1 || a.xrows || a.n_layers < 1 || a.n_layers > kMaxLayers) return 0;
+    if (a.n_used < 1 || a.n_used > kMaxUsed) return 0;
+    if (a.d_model % 512 || a.d_model > 2048 || a.ff % 256 || a.ff > 2048) return 0;
+    if (a.n_layers > 1 && (a.out != a.x || !a.accumulate)) return 0;   // the residual chain
+    if (!a.out || !a.h || !a16(a.x) || !a16(a.out)) return 0;
+    if (a.gu_expert_stride % 16 || a.down_expert_stride % 16) return 0;
+    FlowParams p{};
+    p.rb_gu = (int)sb_row_bytes_of(SB_IQ3_S, a.d_model);
+    p.rb_dn = (int)sb_row_bytes_of(SB_IQ3_S, a.ff);
+    if (16 * p.rb_gu > kStageBytes || 16 * p.rb_dn > kStageBytes || (8 * p.rb_gu) % 16) return 0;
+    p.G = a.d_model / 128;
+    p.Gd = a.ff / 128;
+    if (a.n_used * p.Gd > kMaxDnTasks) return 0;
+    for (int L = 0; L < a.n_layers; ++L)
+        for (const void* b : {a.gate_banks[L], a.up_banks[L], a.down_banks[L]})
+            if (!b || !a16(b)) return 0;
+
+    int dev = 0;
+    if (!sb_cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return -1;
+    if (dev < 0 || dev >= kMaxDev) return 0;
+    if (!g_flow_attr[dev]) {
+        if (!sb_cuda_ok(cudaFuncSetAttribute(k_flow_iq3s, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total),
+                        "flow smem attribute"))
+            return -1;
+        int sms = 0, per_sm = 0;
+        if (!sb_cuda_ok(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count")) return -1;
+        if (!sb_cuda_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_flow_iq3s, kThreads, Smem::total),
+                        "flow occupancy"))
+            return -1;
+        g_flow_grid[dev] = sms * std::min(per_sm, 1);
+        g_flow_attr[dev] = true;
+    }
+    const int grid = g_flow_grid[dev];
+    p.n_units = a.d_model / 16;
+    if (grid < p.n_units) return 0;   // every down unit needs a CTA of its own
+
+    if (!g_fs.mem) {
+        if (!sb_cuda_ok(cudaMalloc(&g_fs.mem, kCtlBytes + kXPairBytes + kHPairBytes), "flow scratch")) return -1;
+        if (!sb_cuda_ok(cudaMemset(g_fs.mem, 0, kCtlBytes + kXPairBytes + kHPairBytes), "flow scratch reset"))
+            return -1;
+    } else if (g_fs.stale) {
+        // a launch that gave up may have left the exit count or the abort word
+        // set; the epoch (word 0) keeps counting so old pairs never match
+        if (!sb_cuda_ok(cudaMemsetAsync((uint8_t*)g_fs.mem + 4, 0, 8, st), "flow scratch reset")) return -1;
+    }
+    g_fs.stale = false;
+    uint8_t* b = (uint8_t*)g_fs.mem;
+    p.ctl = (unsigned*)b;
+    p.xpairs = (unsigned long long*)(b + kCtlBytes);
+    p.hpairs = (unsigned long long*)(b + kCtlBytes + kXPairBytes);
+
+    p.n_layers = a.n_layers;
+    p.n_used = a.n_used;
+    p.n_experts = a.n_experts;
+    p.d_model = a.d_model;
+    p.ff = a.ff;
+    p.n_gu_items = a.n_used * a.ff / 8;
+    p.tps = 2 * 16 * p.rb_dn <= kStageBytes ? 2 : 1;
+    p.n_dn_stages = (a.n_used + p.tps - 1) / p.tps;
+    p.gu_stride = a.gu_expert_stride;
+    p.dn_stride = a.down_expert_stride;
+    p.x = a.x;
+    p.out = a.out;
+    p.accumulate = a.accumulate;
+    p.h = a.h;
+    p.err = a.err;
+    for (int L = 0; L < a.n_layers; ++L) {
+        p.layer[L].gate = (const uint8_t*)a.gate_banks[L];
+        p.layer[L].up = (const uint8_t*)a.up_banks[L];
+        p.layer[L].down = (const uint8_t*)a.down_banks[L];
+        p.layer[L].ids = a.ids + (size_t)L * a.n_used;
+        p.layer[L].w = a.w + (size_t)L * a.n_used;
+    }
+
+    const int tslot = sb_timing_begin("decode_iq3s_flow", st);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Smem::total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_flow_iq3s, p);
+    sb_timing_end(tslot, st);
+    return sb_cuda_ok(e, "flow launch") ? 1 : -1;
+}

@@ -113,6 +113,10 @@ struct sb_decode_args {
 // persistent IQ3_S decode (sb_decode_iq3s.cu): 1 taken, 0 not covered, -1 error
 int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st);
 void sb_decode_scratch_invalidate();
+// barrier-free persistent IQ3_S decode for one token (sb_flow_iq3s.cu), tried
+// first by sb_try_decode_iq3s: 1 taken, 0 not covered, -1 error
+int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st);
+void sb_flow_scratch_invalidate();
 
 // The IQ3_S fused block over a fixed device array instead of allocated scratch
 // (sabah_moe_block_ids_noalloc); -1 with the error set when the call does not fit.

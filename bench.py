@@ -369,10 +369,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (N(0,0.02) weights IQ3_S-encoded on device, N(0,1) router logits)",
-        "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
-                   "top_k": TOP_K, "weights": "IQ3_S", "tokens_per_step": 1,
-                   "l2": "inputs larger than L2: 973 MB of distinct expert bytes per step, 16 routing sets cycled",
-                   "parallelism": "replicas" if world > 1 else "single"},
+        "config": cfg2_config(world),
         "achieved_step_gbs": round(BYTES_PER_TOKEN / (ms_max * 1e-3) / 1e9, 1),
         "roofline": roofline,
         "e2e": {"value": round(world * 1e3 / e_ms, 2), "unit": "tokens/s",
@@ -437,55 +434,70 @@ def cpu_baseline(bank, gate_p, up_p, down_p, ids_np, w_np, use_ref: bool, n_laye
 
 # ---------------------------------------------------------------------------
 # reference arm: the reference's own CPU path (its host dequantizer, compiled
-# from its sources into oracle/_ref) + fp32 dots, all host threads
+# from its sources into oracle/_ref) + fp32 dots, all host threads. Nothing of
+# this repository's library or torch is loaded here.
 # ---------------------------------------------------------------------------
+def iq3s_random_experts(rng, n: int, expert_bytes: int) -> np.ndarray:
+    """n experts of valid IQ3_S blocks (110 B per 256 weights) drawn with numpy:
+    every byte pattern of qs, qh, signs and scales is a valid block; the fp16
+    super-block scale d is drawn so that the weights come out near the product
+    arm's N(0, 0.02) magnitude: mean |w| ~ 0.016 (|w| = d * (1 + 2 * scale) * grid,
+    about 100 d on average for uniform bytes)."""
+    raw = rng.integers(0, 256, size=(n, expert_bytes), dtype=np.uint8)
+    blocks = raw.reshape(n, -1, 110)
+    d = np.abs(rng.normal(1.6e-4, 3e-5, size=blocks.shape[:2])).astype(np.float16)
+    blocks[:, :, 0:2] = d.view(np.uint8).reshape(blocks.shape[0], blocks.shape[1], 2)
+    return raw
+
+
+def cfg2_config(world: int) -> dict:
+    return {"workload": WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+            "top_k": TOP_K, "weights": "IQ3_S", "tokens_per_step": 1,
+            "l2": "inputs larger than L2: 973 MB of distinct expert bytes per step, 16 routing sets cycled",
+            "parallelism": "replicas" if world > 1 else "single"}
+
+
 def run_reference(args, rank: int, world: int, local_rank: int):
     if rank != 0:
         return None
     from oracle import cpu as orc
     if not orc.ref_available():
         return {"impl": "reference", "unavailable": "reference build oracle/_ref/libsabah_rt_ref.so is absent"}
-    import torch
-    from sabah_moe_accelerator_b200 import ops
-    torch.cuda.set_device(local_rank)
-    ops.init(local_rank)
-    n_layers = 4
-    # the same inputs as our arm: the routed experts of the first blocks
-    gate_p, up_p, down_p, keep = [], [], [], []
-    for Lr in range(n_layers):
-        for role, rows, k, lst in ((0, FF, D_MODEL, gate_p), (1, FF, D_MODEL, up_p), (2, D_MODEL, FF, down_p)):
-            t = ops.synth_rows(EXPERTS * rows, k, QT_IQ3_S, seed=(10 + Lr) * 4 + role, sigma=0.02)
-            keep.append(t)
-            lst.append(t.data_ptr())
-    torch.cuda.synchronize()
-    ids_np, w_np = routing(1, n_layers)
-    sample = _host_sample((gate_p, up_p, down_p), ids_np, n_layers)
-    del keep
+    # the routed experts of one token through all LAYERS blocks, in host memory
+    rng = np.random.default_rng(10)
+    gate = iq3s_random_experts(rng, LAYERS * TOP_K, GU_EXPERT).reshape(LAYERS, TOP_K, GU_EXPERT)
+    up = iq3s_random_experts(rng, LAYERS * TOP_K, GU_EXPERT).reshape(LAYERS, TOP_K, GU_EXPERT)
+    down = iq3s_random_experts(rng, LAYERS * TOP_K, D_EXPERT).reshape(LAYERS, TOP_K, D_EXPERT)
+    _, w_np = routing(1, LAYERS)
     threads = os.cpu_count() or 1
-    local_ids = np.tile(np.arange(TOP_K, dtype=np.int32), (n_layers, 1))
+    local_ids = np.tile(np.arange(TOP_K, dtype=np.int32), (LAYERS, 1))
     x = x0()[0]
+    gb = [gate[Lr].ctypes.data for Lr in range(LAYERS)]
+    ub = [up[Lr].ctypes.data for Lr in range(LAYERS)]
+    db = [down[Lr].ctypes.data for Lr in range(LAYERS)]
 
     def step():
-        orc.decode_f32([s[0].ctypes.data for s in sample], [s[1].ctypes.data for s in sample],
-                       [s[2].ctypes.data for s in sample], GU_EXPERT, D_EXPERT, QT_IQ3_S, QT_IQ3_S, local_ids,
-                       w_np[0, :, 0], x, D_MODEL, FF, threads, use_reference_dequant=True)
+        y = orc.decode_f32(gb, ub, db, GU_EXPERT, D_EXPERT, QT_IQ3_S, QT_IQ3_S, local_ids, w_np[0, :, 0], x,
+                           D_MODEL, FF, threads, use_reference_dequant=True)
+        return y
 
     for _ in range(args.warmup):
-        step()
+        y = step()
+    assert np.isfinite(y).all(), "non-finite reference decode"
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     dt = (time.perf_counter() - t0) / args.steps
-    per_token = dt * LAYERS / n_layers
-    v = round(1.0 / per_token, 4)
+    v = round(1.0 / dt, 4)
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_token * 1e3, 3),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (same inputs as the product arm)",
-            "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
-                       "top_k": TOP_K, "weights": "IQ3_S", "tokens_per_step": 1},
+            "data": "synthetic (valid IQ3_S blocks drawn with numpy at the product arm's weight scale; N(0,1) "
+                    "router logits and x as the product arm)",
+            "config": cfg2_config(world),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                             "sample": "each step: one token through %d of 48 blocks, scaled to 48" % n_layers},
+                             "sample": "each step: one token through all %d blocks (10 routed experts each), "
+                                       "reference host dequantizer + fp32 dots" % LAYERS},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -946,6 +958,183 @@ def markov_routing(n_sets: int, n_tok: int, layers: int, p_keep: float = 0.8, se
     return ids, w
 
 
+# cfg 1: Q8_0 decode, one block
+QT_Q8_0 = 8
+Q8_GU_EXPERT = FF * (D_MODEL // 32 * 34)       # 1,671,168
+Q8_D_EXPERT = D_MODEL * (FF // 32 * 34)        # 1,671,168
+Q8_SETS = 16
+Q8_METRIC = "MoE MUL_MAT_ID tokens/s (Q8_0 decode, 1 block, 512 experts, top-10)"
+Q8_WORKLOAD = "cfg1: Q8_0 decode, 1 token x 1 block, 512 experts, top-10, H2048 F768, N(0,0.02) weights (gguf-py's Q8_0 rounding rule)"
+
+
+def run_q8(args, rank: int, world: int, local_rank: int):
+    """cfg 1: one token through one Q8_0 block (gate/up 768 x 2048, down 2048 x
+    768, 512 experts, top-10) through sabah_moe_decode on a device-resident
+    bank; 16 routing sets cycled (about 146 distinct experts, 0.73 GB, so
+    consecutive steps meet cold experts)."""
+    import torch
+    from sabah_moe_accelerator_b200 import ops, rt
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ops.init(local_rank)
+    L = rt.lib()
+    stream = torch.cuda.Stream(device=dev)
+    gate = ops.synth_rows(EXPERTS * FF, D_MODEL, QT_Q8_0, seed=1, sigma=0.02, stream=stream)
+    up = ops.synth_rows(EXPERTS * FF, D_MODEL, QT_Q8_0, seed=2, sigma=0.02, stream=stream)
+    down = ops.synth_rows(EXPERTS * D_MODEL, FF, QT_Q8_0, seed=3, sigma=0.02, stream=stream)
+    stream.synchronize()
+    ids_np, w_np = routing(Q8_SETS, 1)
+    ids_d = torch.from_numpy(ids_np).to(dev)
+    w_d = torch.from_numpy(w_np).to(dev)
+    x0_d = torch.from_numpy(x0()).to(dev)
+    x_d = torch.empty_like(x0_d)
+    h_d = torch.empty((1, TOP_K, FF), dtype=torch.float32, device=dev)
+    c1 = ctypes.c_void_p * 1
+    G, U, D = c1(gate.data_ptr()), c1(up.data_ptr()), c1(down.data_ptr())
+
+    def decode(ids_ptr, w_ptr, st):
+        rt.check(L.sabah_moe_decode(1, G, U, D, Q8_GU_EXPERT, Q8_D_EXPERT, EXPERTS, ids_ptr, w_ptr, x_d.data_ptr(),
+                                    h_d.data_ptr(), D_MODEL, FF, TOP_K, 1, QT_Q8_0, QT_Q8_0, QT_Q8_0,
+                                    st.cuda_stream), "sabah_moe_decode")
+
+    def step(s):
+        x_d.copy_(x0_d)
+        decode(ids_d[s].data_ptr(), w_d[s].data_ptr(), stream)
+
+    # parity of the timed shape: routing set 0 against the fp64 block
+    parity = None
+    if not args.no_parity:
+        from oracle import cpu as orc
+        with torch.cuda.stream(stream):
+            step(0)
+        stream.synchronize()
+        ids0 = ids_np[0, 0, 0]
+        pick = lambda t, per: np.stack([t[int(i) * per:(int(i) + 1) * per].cpu().numpy() for i in ids0])
+        y = orc.moe_block_f64(pick(gate, Q8_GU_EXPERT), pick(up, Q8_GU_EXPERT), pick(down, Q8_D_EXPERT),
+                              np.arange(TOP_K, dtype=np.int32), w_np[0, 0, 0], x0()[0], D_MODEL, FF, QT_Q8_0,
+                              QT_Q8_0, QT_Q8_0)
+        parity = float(orc.rel_l2(x_d.cpu().numpy()[0], x0()[0].astype(np.float64) + y))
+        if not parity <= 2e-3:
+            raise SystemExit("cfg1 parity failed: rel-L2 %.3e against fp64" % parity)
+
+    with torch.cuda.stream(stream):
+        for s in range(Q8_SETS):
+            step(s)
+    stream.synchronize()
+    graphs = []
+    with torch.cuda.stream(stream):
+        for s in range(Q8_SETS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(s)
+            graphs.append(g)
+    stream.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % Q8_SETS].replay()
+    stream.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(args.steps):
+            graphs[i % Q8_SETS].replay()
+        t1.record(stream)
+    stream.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+
+    timing_steps = 8
+    L.sabah_rt_kernel_timing(1)
+    with torch.cuda.stream(stream):
+        for i in range(timing_steps):
+            step(i % Q8_SETS)
+    stream.synchronize()
+    buf = ctypes.create_string_buffer(8192)
+    L.sabah_rt_kernel_times(buf, 8192)
+    L.sabah_rt_kernel_timing(0)
+    ktimes = json.loads(buf.value.decode())
+    launches_per_step = sum(v[0] for v in ktimes.values()) / timing_steps
+    # algorithmic bytes per token: the 10 routed experts once, plus activations
+    step_bytes = TOP_K * (2 * Q8_GU_EXPERT + Q8_D_EXPERT) + 2 * D_MODEL * 4 + 2 * TOP_K * FF * 4
+    peaks, peak_kind = measured_peaks()
+    dev_ms = sum(v[1] for v in ktimes.values()) / timing_steps
+    dom_name, dom = max(ktimes.items(), key=lambda kv: kv[1][1])
+    achieved = step_bytes / (dev_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "+".join(sorted(ktimes)), "achieved": round(achieved, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": None, "peak_kind": peak_kind, "bytes_per_launch": int(step_bytes),
+                "avg_launch_us": round(dev_ms * 1e3, 2), "note": "all kernels of a step together (one block)",
+                "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)} for k, v in ktimes.items()}}
+
+    x0_h = torch.from_numpy(x0()).pin_memory()
+    ids_h = torch.from_numpy(ids_np).pin_memory()
+    w_h = torch.from_numpy(w_np).pin_memory()
+    out_h = torch.empty((1, D_MODEL), dtype=torch.float32).pin_memory()
+    ids_cur, w_cur = torch.empty_like(ids_d[0]), torch.empty_like(w_d[0])
+
+    def e2e_step(s):
+        x_d.copy_(x0_h, non_blocking=True)
+        ids_cur.copy_(ids_h[s], non_blocking=True)
+        w_cur.copy_(w_h[s], non_blocking=True)
+        decode(ids_cur.data_ptr(), w_cur.data_ptr(), stream)
+        out_h.copy_(x_d, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            e2e_step(i % Q8_SETS)
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, args.steps)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            e2e_step(i % Q8_SETS)
+        e1.record(stream)
+    stream.synchronize()
+    e_ms = e0.elapsed_time(e1) / e2e_steps
+    assert np.isfinite(out_h.numpy()).all(), "non-finite decode output"
+    res = {
+        "metric": Q8_METRIC, "value": round(1e3 / ms, 2), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (N(0,0.02) weights Q8_0-encoded on device, N(0,1) router logits and x)",
+        "config": {"workload": Q8_WORKLOAD, "layers": 1, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+                   "top_k": TOP_K, "weights": "Q8_0", "tokens_per_step": 1,
+                   "l2": "inputs larger than L2 across steps: %d routing sets cycled over 2.57 GB of experts" % Q8_SETS},
+        "achieved_step_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1),
+        "roofline": roofline,
+        "e2e": {"value": round(1e3 / e_ms, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x0_h.numel() * 4 + ids_h[0].numel() * 4 + w_h[0].numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
+                "path": "sabah_moe_decode (C ABI), eager launches"},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "clocks": clk,
+        "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3, "checked": "routing set 0, before timing"}
+        if parity is not None else None,
+    }
+    if not args.no_cpu_baseline:
+        from oracle import cpu as orc
+        ids0 = ids_np[0, 0, 0]
+        hs = [np.ascontiguousarray(np.stack([t[int(i) * per:(int(i) + 1) * per].cpu().numpy() for i in ids0]))
+              for t, per in ((gate, Q8_GU_EXPERT), (up, Q8_GU_EXPERT), (down, Q8_D_EXPERT))]
+        threads = os.cpu_count() or 1
+        t_0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t_0 < 5.0 and reps < 200:
+            orc.decode_f32([hs[0].ctypes.data], [hs[1].ctypes.data], [hs[2].ctypes.data], Q8_GU_EXPERT, Q8_D_EXPERT,
+                           QT_Q8_0, QT_Q8_0, np.arange(TOP_K, dtype=np.int32)[None], w_np[0, :1, 0], x0()[0],
+                           D_MODEL, FF, threads)
+            reps += 1
+        dt = (time.perf_counter() - t_0) / reps
+        res["cpu_baseline"] = {"value": round(1.0 / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                               "sample": "the timed token (routing set 0), %d repetitions" % reps}
+    del graphs
+    return res
+
+
 def run_mixed(args, rank: int, world: int, local_rank: int):
     """cfg 4: 4 tokens through 48 Q4_K/Q6_K blocks per step, through
     sabah_moe_decode on a device-resident bank."""
@@ -1111,8 +1300,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the fp64 check of the timed shape that runs before timing (profiling only)")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg3", "cfg4", "cfg5", "cfg5s"],
-                    help="cfg2: the headline 1-token decode (replicas for N > 1); cfg3: 512-token prefill "
+    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "cfg5s"],
+                    help="cfg1: Q8_0 1-token decode of one block; "
+                         "cfg2: the headline 1-token decode (replicas for N > 1); cfg3: 512-token prefill "
                          "of one block; cfg4: Q4_K/Q6_K batch-4 decode; cfg5: expert-parallel bank; cfg5s: "
                          "host-resident bank streamed through the hot-tier slab")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -1142,6 +1332,8 @@ def main():
         res = run_prefill(args, rank, world, local_rank) if rank == 0 else None
     elif args.workload == "cfg4":
         res = run_mixed(args, rank, world, local_rank) if rank == 0 else None
+    elif args.workload == "cfg1":
+        res = run_q8(args, rank, world, local_rank) if rank == 0 else None
     elif args.workload == "cfg5s":
         res = run_stream(args, rank, world, local_rank) if rank == 0 else None
     else:

@@ -43,16 +43,17 @@
 #include <cstdio>
 #include <cstdlib>
 
-#include "sb_iq3s_core.cuh"
+#include "sb_flow_core.cuh"
 
 namespace {
 
 using namespace sb_iq3s;
+using namespace sb_flow;
 
 constexpr int kNC = 16;                      // consumer warps
-constexpr int kThreads = (kNC + 1) * 32;     // + one producer warp
-constexpr int kLogR = 5;                     // 32 grid-table replicas: conflict-free lookups
-constexpr int kR = 1 << kLogR;
+constexpr int kProducer = kNC;               // warp 16 streams tiles
+constexpr int kEpilogue = kNC + 1;           // warp 17 reduces, publishes and releases stages
+constexpr int kThreads = (kNC + 2) * 32;
 constexpr int kStageBytes = 16 * 880;        // a stacked gate/up tile at d_model <= 2048
 constexpr int kStages = 9;                   // = issuing producer lanes: lane l owns stage l
 constexpr int kMaxLayers = 64;               // tags hold the layer in 6 bits
@@ -66,19 +67,19 @@ struct Desc {
     int a, b;   // gate/up: slot, 8-row block; down: first slot, tiles
 };
 
+// A stage's use ends in two steps: its consumers arrive on done[s] (16
+// arrivals per use) once their partial rows are in shared memory; the
+// epilogue warp then reduces them and arrives on empty[s] for the producer.
 struct Smem {
     static constexpr int table = 0;
-    static constexpr int stages = table + table_bytes<kR>();
+    static constexpr int stages = table + kGridBytes;
     static constexpr int red = stages + kStages * kStageBytes;          // [kStages][kNC][16] float
     static constexpr int dred = red + kStages * kNC * 16 * 4;          // [kMaxDnTasks][16] float
     static constexpr int bst = dred + kMaxDnTasks * 16 * 4;            // [kNC][32][16 B] B staging
-    static constexpr int xown = bst + kNC * 512;                       // [16] float: the unit's x rows
-    static constexpr int desc = xown + 16 * 4;                         // [kStages] Desc
-    static constexpr int cnt = desc + kStages * (int)sizeof(Desc);     // [kStages] int
-    static constexpr int ucnt = cnt + kStages * 4;                     // int: finished down tasks
-    static constexpr int abort_flag = ucnt + 4;
-    static constexpr int bars = (abort_flag + 4 + 7) & ~7;             // full[kStages], empty[kStages]
-    static constexpr int total = bars + 2 * kStages * 8;
+    static constexpr int desc = bst + kNC * 512;                       // [kStages] Desc
+    static constexpr int abort_flag = desc + kStages * (int)sizeof(Desc);
+    static constexpr int bars = (abort_flag + 4 + 7) & ~7;             // full, empty, done [kStages] each
+    static constexpr int total = bars + 3 * kStages * 8;
 };
 static_assert(Smem::total <= 227 * 1024, "shared memory budget");
 static_assert(Smem::stages % 128 == 0 && kStageBytes % 128 == 0, "stage alignment");
@@ -107,12 +108,20 @@ struct FlowParams {
     float* h;                  // [n_used][ff]: h of the last block
     unsigned long long* xpairs;   // [2][d_model]
     unsigned long long* hpairs;   // [2][n_used][ff]
-    unsigned* ctl;             // [0] epoch, [1] CTAs exited, [2] global abort
+    unsigned* ctl;             // [0] epoch, [1] CTAs exited, [2] global abort; [64..) never written
     int* err;
+    // test only (SABAH_TEST_FLOW_STALL): CTA 0 first waits, with a short poll
+    // limit, for pairs that nothing writes, so the kernel must give up, record
+    // SB_DERR_TIMEOUT and return; the next call runs clean
+    int stall_test;
     FlowLayer layer[kMaxLayers];
 };
 
-__device__ inline void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kNC * 32) : "memory"); }
+// consumers and the epilogue warp (not the producer, which leaves early)
+__device__ inline void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"((kNC + 1) * 32) : "memory"); }
+__device__ inline void mbar_arrive_n(uint32_t bar, uint32_t n) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(n) : "memory");
+}
 
 __device__ inline unsigned ld_relaxed_u32(const unsigned* p) {
     unsigned v;
@@ -133,8 +142,15 @@ __device__ inline void give_up(volatile int* abort_flag, unsigned* gabort, int* 
     st_relaxed_u32(gabort, 1u);
     if (err) atomicExch(err, SB_DERR_TIMEOUT);
 }
+// Another CTA's give-up is adopted as this CTA's own, so its local waits
+// (stage barriers, stamps) end at once too.
 __device__ inline bool aborting(volatile int* abort_flag, const unsigned* gabort) {
-    return *abort_flag || ld_relaxed_u32(gabort);
+    if (*abort_flag) return true;
+    if (ld_relaxed_u32(gabort)) {
+        *abort_flag = 1;
+        return true;
+    }
+    return false;
 }
 // Warp-uniform forms: every lane of the warp gets the same answer, so the
 // warp never splits before a shuffle, a vote or mma.sync.
@@ -151,9 +167,9 @@ __device__ inline bool warp_wait_stage(const int* stamp, int seq, uint32_t full,
 // values once all 32 lanes see `tag` on all four. False if the kernel is
 // aborting or the wait gives up.
 __device__ inline bool poll4(const unsigned long long* p, unsigned tag, float4& out, volatile int* abort_flag,
-                             unsigned* gabort, int* err) {
+                             unsigned* gabort, int* err, long long limit = kPollLimit) {
     const unsigned long long* q = p + 4 * (threadIdx.x & 31);
-    for (long long i = 0; i < kPollLimit; ++i) {
+    for (long long i = 0; i < limit; ++i) {
         unsigned long long v0, v1, v2, v3;
         asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "l"(q) : "memory");
         asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v2), "=l"(v3) : "l"(q + 2) : "memory");
@@ -171,141 +187,6 @@ __device__ inline bool poll4(const unsigned long long* p, unsigned tag, float4& 
     return false;
 }
 
-// B fragments of mma.sync m16n8k16 for one 128-element group of a vector, lane
-// l holding elements [4l, 4l + 4): per sub-block (8 lanes) a power-of-two
-// scale puts the max into [2^13, 2^14); each value splits into fp16 hi and lo.
-// Lane (g, c) gets, for step S, the hi (g even) or lo (g odd) pairs of entry S
-// of sub-block c when g / 2 == c, zeros otherwise (the K permutation of the
-// decode core), and inv = 2^24 / scale of sub-block c.
-__device__ inline void build_b(float4 v4, uint32_t bst, uint32_t (&bf)[8][2], float& inv) {
-    const int lane = threadIdx.x & 31;
-    float m = fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w)));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-    int ex = 0;
-    if (m > 0.f && isfinite(m)) {
-        frexpf(m, &ex);   // m = f * 2^ex, f in [0.5, 1)
-        ex = max(-100, min(100, 14 - ex));
-    }
-    const float s = ldexpf(1.f, ex);
-    const float v[4] = {v4.x * s, v4.y * s, v4.z * s, v4.w * s};
-    __half hi[4], lo[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        hi[i] = __float2half_rn(v[i]);
-        lo[i] = __float2half_rn(v[i] - __half2float(hi[i]));
-    }
-    const __half2 h01 = __halves2half2(hi[0], hi[1]), h23 = __halves2half2(hi[2], hi[3]);
-    const __half2 l01 = __halves2half2(lo[0], lo[1]), l23 = __halves2half2(lo[2], lo[3]);
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(bst + 16u * lane), "r"(*(const uint32_t*)&h01),
-                 "r"(*(const uint32_t*)&h23), "r"(*(const uint32_t*)&l01), "r"(*(const uint32_t*)&l23)
-                 : "memory");
-    const float my_inv = 16777216.0f / s;   // 2^24 undoes the subnormal encoding of the weights
-    __syncwarp();
-    const int g = lane >> 2, c = lane & 3;
-    inv = __shfl_sync(0xffffffffu, my_inv, 8 * c);
-    const bool mine = (g >> 1) == c;
-    const uint32_t src = bst + 16u * (8 * c) + 8u * (g & 1);
-#pragma unroll
-    for (int S = 0; S < 8; ++S) {
-        uint32_t b0 = 0, b1 = 0;
-        if (mine) asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(src + 16u * S));
-        bf[S][0] = b0;
-        bf[S][1] = b1;
-    }
-    __syncwarp();   // the staging area may be rewritten after this
-}
-
-// Fields of rows g (h = 0) and g + 8 (h = 1) for sub-block 4N + c of the
-// super-block at shared address sb (row 0): 8 qs bytes (4 u16), 4 sign
-// bytes, the qh byte spread to one 0/1 byte per entry, and the scale
-// db = d * (1 + 2 * nibble) * inv.
-template <int N>
-__device__ inline void fields(uint32_t sb, const Lane& L, float inv, uint32_t (&qsw)[2][4], uint32_t (&QH)[2][2],
-                              uint32_t (&sgw)[2][4], float (&db)[2]) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint32_t r8 = sb + L.row8c + h * L.rb8, r4 = sb + L.row4c + h * L.rb8;
-        const uint32_t r1 = sb + L.row1c + h * L.rb8, rh = sb + L.rowhc + h * L.rb8;
-        const float d = __half2float(__ushort_as_half((unsigned short)ld_u16<0>(sb + L.row0 + h * L.rb8)));
-        qsw[h][0] = ld_u16<2 + 32 * N>(r8);
-        qsw[h][1] = ld_u16<4 + 32 * N>(r8);
-        qsw[h][2] = ld_u16<6 + 32 * N>(r8);
-        qsw[h][3] = ld_u16<8 + 32 * N>(r8);
-        sgw[h][0] = ld_u8<74 + 16 * N>(r4);
-        sgw[h][1] = ld_u8<75 + 16 * N>(r4);
-        sgw[h][2] = ld_u8<76 + 16 * N>(r4);
-        sgw[h][3] = ld_u8<77 + 16 * N>(r4);
-        const uint32_t qh = ld_u8<66 + 4 * N>(r1);
-        QH[h][0] = ((qh & 15u) * 0x00204081u) & 0x01010101u;   // qh bits 0..3 -> bytes 0..3
-        QH[h][1] = ((qh >> 4) * 0x00204081u) & 0x01010101u;    // qh bits 4..7 -> bytes 0..3
-        const uint32_t nib = (ld_u8<106 + 2 * N>(rh) >> L.nib_shift) & 15u;
-        db[h] = d * (float)(1 + 2 * (int)nib) * inv;
-    }
-}
-
-// Step S (grid entry S of the lane's sub-block) for rows g and g + 8: decode
-// into A fragments and issue the MMA into accumulator S & 1.
-template <int S>
-__device__ inline void step1(uint32_t table, const uint32_t (&qsw)[2][4], const uint32_t (&QH)[2][2],
-                             const uint32_t (&sgw)[2][4], const uint32_t (&bf)[8][2], float (&dd)[2][4]) {
-    // PRMT selector: byte 0 = qs byte (S & 1) of the u16 word, byte 1 = QH byte (S & 3), bytes 2, 3 = 0
-    constexpr uint32_t sel = (uint32_t)(S & 1) | ((4u + (S & 3)) << 4) | (2u << 8) | (2u << 12);
-    constexpr uint32_t mask = (S & 1) ? 0xF0u : 0x0Fu;                 // entry S's sign nibble
-    constexpr uint32_t kspread = (S & 1) ? 0x01020408u : 0x10204080u;  // nibble bits -> bit 7 of bytes 0..3
-    uint32_t a[2][2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const uint32_t idx = prmt(qsw[h][S >> 1], QH[h][S >> 2], sel);
-        uint32_t grid;
-        asm("ld.shared.u32 %0, [%1];" : "=r"(grid) : "r"((idx << (kLogR + 2)) + table));
-        const uint32_t Z = ((sgw[h][S >> 1] & mask) * kspread) & 0x80808080u;
-        a[h][0] = prmt(grid, Z, 0x5140);   // (e0, e1) as signed fp16 subnormals
-        a[h][1] = prmt(grid, Z, 0x7362);   // (e2, e3)
-    }
-    mma16816(dd[S & 1], a[0][0], a[1][0], a[0][1], a[1][1], bf[S][0], bf[S][1]);
-}
-
-// One 128-weight group (sub-blocks 4N .. 4N + 3 of the super-block at sb) of a
-// 16-row tile: adds the dots of rows g and g + 8 (this lane's sub-block) to acc.
-template <int N>
-__device__ inline void do_group(uint32_t sb, const Lane& L, const uint32_t (&bf)[8][2], float inv, float (&acc)[2]) {
-    uint32_t qsw[2][4], QH[2][2], sgw[2][4];
-    float db[2];
-    fields<N>(sb, L, inv, qsw, QH, sgw, db);
-    float dd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    step1<0>(L.table, qsw, QH, sgw, bf, dd);
-    step1<1>(L.table, qsw, QH, sgw, bf, dd);
-    step1<2>(L.table, qsw, QH, sgw, bf, dd);
-    step1<3>(L.table, qsw, QH, sgw, bf, dd);
-    step1<4>(L.table, qsw, QH, sgw, bf, dd);
-    step1<5>(L.table, qsw, QH, sgw, bf, dd);
-    step1<6>(L.table, qsw, QH, sgw, bf, dd);
-    step1<7>(L.table, qsw, QH, sgw, bf, dd);
-    acc[0] = fmaf(db[0], (dd[0][0] + dd[0][1]) + (dd[1][0] + dd[1][1]), acc[0]);
-    acc[1] = fmaf(db[1], (dd[0][2] + dd[0][3]) + (dd[1][2] + dd[1][3]), acc[1]);
-}
-
-// group q of a row: super-block q / 2, half q % 2
-__device__ inline void do_group_q(uint32_t tile, int q, const Lane& L, const uint32_t (&bf)[8][2], float inv,
-                                  float (&acc)[2]) {
-    const uint32_t sb = tile + (uint32_t)(q >> 1) * 110u;
-    if (q & 1)
-        do_group<1>(sb, L, bf, inv, acc);
-    else
-        do_group<0>(sb, L, bf, inv, acc);
-}
-
-// rows g, g + 8 of the quad's partial sums, summed over the quad (c = 0..3)
-__device__ inline void quad_sum(float (&acc)[2]) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 1);
-        acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], 2);
-    }
-}
-
 // Gate/up items go round-robin over the CTAs in reverse order (item i to CTA
 // grid - 1 - i % grid), so the CTAs that get one item more than the rest
 // include those without a down unit (the units take CTAs 0 .. n_units - 1).
@@ -320,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
     uint64_t* bars = (uint64_t*)(smem + Smem::bars);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kStages), done0 = smem_u32(bars + 2 * kStages);
     volatile int* abort_flag = (volatile int*)(smem + Smem::abort_flag);
     Desc* descs = (Desc*)(smem + Smem::desc);
     unsigned* gabort = p.ctl + 2;
@@ -331,20 +212,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
 
     if (threadIdx.x == 0) {
         *abort_flag = 0;
-        *(int*)(smem + Smem::ucnt) = 0;
         for (int s = 0; s < kStages; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, 1);   // one release per use, by the stage's last user
+            mbar_init(empty0 + 8 * s, 1);     // the epilogue warp, once per use
+            mbar_init(done0 + 8 * s, kNC);    // 16 arrivals per use (see the consumers)
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (threadIdx.x < kStages) {
-        ((int*)(smem + Smem::cnt))[threadIdx.x] = 0;
-        descs[threadIdx.x].seq = -1;
-    }
+    if (threadIdx.x < kStages) descs[threadIdx.x].seq = -1;
     __syncthreads();
 
-    if (warp == kNC) {
+    if (warp == kProducer) {
         // ------------------------------------------------------------ producer
         // lane l issues this CTA's sequence numbers n = l, l + kStages, ...
         // over all layers, always into stage l
@@ -427,152 +305,197 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
         return;
     }
 
-    // -------------------------------------------------------------- consumers
-    uint32_t* table = (uint32_t*)(smem + Smem::table);
-    fill_table<kNC * 32, kR>(table);
-    consumers_sync();
-    const int g = lane >> 2, c = lane & 3;
-    const Lane Lg = lane_init<kR>(table, p.rb_gu, lane);
-    const Lane Ld = lane_init<kR>(table, p.rb_dn, lane);
-    const uint32_t stages32 = smem_u32(smem + Smem::stages);
-    const uint32_t bst = smem_u32(smem + Smem::bst) + 512u * warp;
     float* red = (float*)(smem + Smem::red);
     float* dred = (float*)(smem + Smem::dred);
-    float* xown = (float*)(smem + Smem::xown);
-    int* cnt = (int*)(smem + Smem::cnt);
-    int* ucnt = (int*)(smem + Smem::ucnt);
     const unsigned epoch = ld_relaxed_u32(p.ctl);
     const int n_tasks = p.n_used * p.Gd;
     const float nan = __int_as_float(0x7fc00000);
 
-    for (int L = 0; L < p.n_layers; ++L) {
-        const unsigned tag = (epoch << 6) + (unsigned)L + 1u;
-        const FlowLayer& lb = p.layer[L];
-        const int seq0 = L * per;
-        // ------------------------------------------------ gate/up: group `warp` of every item
-        if (warp < p.G && ng > 0) {
-            uint32_t bf[8][2];
-            float inv = 0.f;
-            float4 xv;
-            bool have;
-            if (L == 0) {
-                xv = __ldcg((const float4*)(p.x + 128 * warp) + lane);
-                have = !warp_aborting(abort_flag, gabort);
-            } else {
-                have = poll4(p.xpairs + (size_t)(L & 1) * p.d_model + 128 * warp, tag, xv, abort_flag, gabort, p.err);
-            }
-            if (have) build_b(xv, bst, bf, inv);
-            for (int k = 0; k < ng && have; ++k) {
-                const int n = seq0 + k, s = n % kStages;
-                if (!warp_wait_stage(&descs[s].seq, n, full0 + 8 * s, (n / kStages) & 1, p.err, abort_flag)) {
-                    have = false;
-                    break;
-                }
+    if (warp == kEpilogue) {
+        // ------------------------------------------------------------ epilogue
+        // walks this CTA's stage uses in order: once the 16 arrivals of a use are
+        // in, gate/up: sums the warps' partial rows in warp order and publishes
+        // h = silu(g) * u; every use: releases the stage to the producer. After
+        // the down stages of a layer: the unit's combine, x_{L+1} = x_L + y.
+        consumers_sync();
+        const int r = lane & 15;
+        const int row = cta * 16 + r;
+        float xr = 0.f;
+        if (nd > 0) xr = p.accumulate ? p.out[row] : 0.f;
+        bool ok = true;
+        for (int L = 0; L < p.n_layers && ok; ++L) {
+            const unsigned tag = (epoch << 6) + (unsigned)L + 1u;
+            const FlowLayer& lb = p.layer[L];
+            for (int k = 0; k < per && ok; ++k) {
+                const int n = L * per + k, s = n % kStages;
+                ok = __all_sync(0xffffffffu, mbar_wait(done0 + 8 * s, (n / kStages) & 1, p.err, abort_flag));
+                if (!ok) break;
                 const Desc d = descs[s];
-                float acc[2] = {0.f, 0.f};
-                if (!d.bad) do_group_q(stages32 + s * kStageBytes, warp, Lg, bf, inv, acc);
-                quad_sum(acc);
-                float* rr = red + (s * kNC + warp) * 16;
-                if (c == 0) {
-                    rr[g] = acc[0];
-                    rr[g + 8] = acc[1];
+                if (k < ng) {
+                    float v = 0.f;
+                    if (lane < 16)
+                        for (int w = 0; w < p.G; ++w) v += red[(s * kNC + w) * 16 + lane];
+                    const float u = __shfl_sync(0xffffffffu, v, (lane + 8) & 31);
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(empty0 + 8 * s);   // the tile and its partial rows are consumed
+                        if (d.bad && p.err) atomicExch(p.err, SB_DERR_BAD_ID);
+                    }
+                    if (lane < 8) {
+                        const float hv = d.bad ? nan : v / (1.f + expf(-v)) * u;
+                        const size_t hrow = (size_t)d.a * p.ff + (size_t)d.b * 8 + lane;
+                        st_pair(p.hpairs + (size_t)(L & 1) * p.n_used * p.ff + hrow, hv, tag);
+                        p.h[hrow] = hv;
+                    }
+                } else {
+                    if (lane == 0) {
+                        mbar_arrive(empty0 + 8 * s);
+                        if (d.bad && p.err) atomicExch(p.err, SB_DERR_BAD_ID);
+                    }
                 }
-                __threadfence_block();
-                __syncwarp();
-                int lastw = 0;
-                if (lane == 0) lastw = atomicAdd(cnt + s, 1) == p.G - 1;
-                lastw = __shfl_sync(0xffffffffu, lastw, 0);
-                if (!lastw) continue;
-                // ---- the item's last warp: rows in fixed warp order, then h = silu(g) * u
-                __threadfence_block();
+            }
+            if (!ok || nd == 0) continue;
+            // every task of the unit is done: groups in order, slots in order (weighted)
+            float tot = 0.f;
+            for (int e2 = 0; e2 < p.n_used; ++e2) {
                 float v = 0.f;
-                if (lane < 16)
-                    for (int w = 0; w < p.G; ++w) v += red[(s * kNC + w) * 16 + lane];
-                const float u = __shfl_sync(0xffffffffu, v, (lane + 8) & 31);
-                __syncwarp();
-                if (lane == 0) {
-                    cnt[s] = 0;
-                    __threadfence_block();
-                    mbar_arrive(empty0 + 8 * s);   // the tile and its partial rows are consumed
-                    if (d.bad && p.err) atomicExch(p.err, SB_DERR_BAD_ID);
-                }
-                if (lane < 8) {
-                    const float hv = d.bad ? nan : v / (1.f + expf(-v)) * u;
-                    const size_t row = (size_t)d.a * p.ff + (size_t)d.b * 8 + lane;
-                    st_pair(p.hpairs + (size_t)(L & 1) * p.n_used * p.ff + row, hv, tag);
-                    p.h[row] = hv;
-                }
+                for (int j2 = 0; j2 < p.Gd; ++j2) v += dred[(e2 * p.Gd + j2) * 16 + r];
+                tot += __ldg(lb.w + e2) * v;
+            }
+            xr = xr + tot;
+            __syncwarp();   // dred is read before the next layer's tasks may write it
+            if (lane < 16) {
+                if (L + 1 < p.n_layers)
+                    st_pair(p.xpairs + (size_t)((L + 1) & 1) * p.d_model + row, xr, tag + 1u);
+                else
+                    p.out[row] = xr;
             }
         }
-        // ------------------------------------------------ down: tasks (slot, group) of this CTA's unit
-        if (nd > 0) {
-            const int unit = cta;
-            for (int t = warp; t < n_tasks; t += kNC) {
-                if (warp_aborting(abort_flag, gabort)) break;
-                const int e = t / p.Gd, j = t % p.Gd;
-                const int ds = e / p.tps, n = seq0 + ng + ds, s = n % kStages;
-                float4 hv;
-                if (!poll4(p.hpairs + (size_t)(L & 1) * p.n_used * p.ff + (size_t)e * p.ff + 128 * j, tag, hv,
-                           abort_flag, gabort, p.err))
-                    break;
+    } else {
+        // ------------------------------------------------------------ consumers
+        uint32_t* table = (uint32_t*)(smem + Smem::table);
+        fill_grid<kNC * 32>(table);
+        consumers_sync();
+        const uint32_t tab = grid_lane(table, lane);
+        const int g = lane >> 2, c = lane & 3;
+        const Lane Lg = lane_init<kR>(table, p.rb_gu, lane);
+        const Lane Ld = lane_init<kR>(table, p.rb_dn, lane);
+        const uint32_t stages32 = smem_u32(smem + Smem::stages);
+        const uint32_t bst = smem_u32(smem + Smem::bst) + 512u * warp;
+        // warp 0 supplies the arrivals of the gate/up warps that do not exist (G < 16)
+        const uint32_t gu_arrivals = warp == 0 ? 1u + (uint32_t)(kNC - p.G) : 1u;
+
+        for (int L = 0; L < p.n_layers; ++L) {
+            const unsigned tag = (epoch << 6) + (unsigned)L + 1u;
+            const int seq0 = L * per;
+            // -------------------------------------------- gate/up: group `warp` of every item, two at a time
+            if (warp < p.G && ng > 0) {
                 uint32_t bf[8][2];
-                float inv;
-                build_b(hv, bst, bf, inv);
-                if (!warp_wait_stage(&descs[s].seq, n, full0 + 8 * s, (n / kStages) & 1, p.err, abort_flag)) break;
-                const Desc d = descs[s];
-                const int tl = e - d.a;
-                const bool bad = (d.bad >> tl) & 1;
-                float acc[2] = {0.f, 0.f};
-                if (!bad)
-                    do_group_q(stages32 + s * kStageBytes + (uint32_t)tl * 16u * p.rb_dn, j, Ld, bf, inv, acc);
-                quad_sum(acc);
-                if (c == 0) {
-                    dred[t * 16 + g] = bad ? nan : acc[0];
-                    dred[t * 16 + g + 8] = bad ? nan : acc[1];
+                float inv = 0.f;
+                float4 xv;
+                bool have;
+                if (L == 0) {
+                    xv = __ldcg((const float4*)(p.x + 128 * warp) + lane);
+                    have = !warp_aborting(abort_flag, gabort);
+                    if (p.stall_test && cta == 0 && have)
+                        have = poll4((const unsigned long long*)(p.ctl + 64), tag, xv, abort_flag, gabort, p.err,
+                                     1ll << 12);
+                } else {
+                    have = poll4(p.xpairs + (size_t)(L & 1) * p.d_model + 128 * warp, tag, xv, abort_flag, gabort,
+                                 p.err);
                 }
-                __threadfence_block();
-                __syncwarp();
-                int ulast = 0;
-                if (lane == 0) {
-                    // release the stage once all its tasks are done
-                    const int in_stage = d.b * p.Gd;
-                    if (atomicAdd(cnt + s, 1) == in_stage - 1) {
-                        cnt[s] = 0;
-                        __threadfence_block();
-                        mbar_arrive(empty0 + 8 * s);
+                if (have) build_b(xv, bst, bf, inv);
+                for (int k = 0; k < ng && have; k += 2) {
+                    const int n0 = seq0 + k, s0 = n0 % kStages;
+                    const bool two = k + 1 < ng;
+                    const int n1 = n0 + 1, s1 = n1 % kStages;
+                    if (!warp_wait_stage(&descs[s0].seq, n0, full0 + 8 * s0, (n0 / kStages) & 1, p.err,
+                                         abort_flag) ||
+                        (two && !warp_wait_stage(&descs[s1].seq, n1, full0 + 8 * s1, (n1 / kStages) & 1, p.err,
+                                                 abort_flag))) {
+                        have = false;
+                        break;
                     }
-                    if (bad && p.err) atomicExch(p.err, SB_DERR_BAD_ID);
-                    ulast = atomicAdd(ucnt, 1) == n_tasks - 1;
+                    const bool bad0 = descs[s0].bad != 0, bad1 = two && descs[s1].bad != 0;
+                    const uint32_t t0 = stages32 + s0 * kStageBytes, t1 = stages32 + s1 * kStageBytes;
+                    float a0[2] = {0.f, 0.f}, a1[2] = {0.f, 0.f};
+                    if (two && !bad0 && !bad1) {
+                        do_group2_q(t0, t1, warp, Lg, tab, bf, inv, a0, a1);
+                    } else {
+                        if (!bad0) do_group_q(t0, warp, Lg, tab, bf, inv, a0);
+                        if (two && !bad1) do_group_q(t1, warp, Lg, tab, bf, inv, a1);
+                    }
+                    quad_sum(a0);
+                    quad_sum(a1);
+                    if (c == 0) {
+                        float* r0 = red + (s0 * kNC + warp) * 16;
+                        r0[g] = a0[0];
+                        r0[g + 8] = a0[1];
+                        if (two) {
+                            float* r1 = red + (s1 * kNC + warp) * 16;
+                            r1[g] = a1[0];
+                            r1[g + 8] = a1[1];
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive_n(done0 + 8 * s0, gu_arrivals);
+                        if (two) mbar_arrive_n(done0 + 8 * s1, gu_arrivals);
+                    }
                 }
-                ulast = __shfl_sync(0xffffffffu, ulast, 0);
-                if (!ulast) continue;
-                // ---- the unit's last task: groups in order, slots in order (weighted), residual
-                __threadfence_block();
-                const int r = lane & 15;
-                const int row = unit * 16 + r;
-                float tot = 0.f;
-                for (int e2 = 0; e2 < p.n_used; ++e2) {
-                    float v = 0.f;
-                    for (int j2 = 0; j2 < p.Gd; ++j2) v += dred[(e2 * p.Gd + j2) * 16 + r];
-                    tot += __ldg(lb.w + e2) * v;
+            }
+            // -------------------------------------------- down: tasks (slot, group) of this CTA's unit
+            if (nd > 0 && warp < n_tasks) {
+                const unsigned long long* hbase = p.hpairs + (size_t)(L & 1) * p.n_used * p.ff;
+                // the first task's pairs are requested before anything waits on them
+                unsigned long long pv[4];
+                auto request = [&](int t) {
+                    const unsigned long long* q =
+                        hbase + (size_t)(t / p.Gd) * p.ff + 128 * (t % p.Gd) + 4 * lane;
+                    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[0]), "=l"(pv[1]) : "l"(q)
+                                 : "memory");
+                    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[2]), "=l"(pv[3])
+                                 : "l"(q + 2)
+                                 : "memory");
+                };
+                request(warp);
+                for (int t = warp; t < n_tasks; t += kNC) {
+                    const int e = t / p.Gd, j = t % p.Gd;
+                    const int ds = e / p.tps, n = seq0 + ng + ds, s = n % kStages;
+                    // the requested pairs, if they already carry this layer's tag; else poll
+                    float4 hv;
+                    const bool ready = (unsigned)(pv[0] >> 32) == tag && (unsigned)(pv[1] >> 32) == tag &&
+                                       (unsigned)(pv[2] >> 32) == tag && (unsigned)(pv[3] >> 32) == tag;
+                    if (__all_sync(0xffffffffu, ready)) {
+                        hv = make_float4(__uint_as_float((unsigned)pv[0]), __uint_as_float((unsigned)pv[1]),
+                                         __uint_as_float((unsigned)pv[2]), __uint_as_float((unsigned)pv[3]));
+                    } else if (!poll4(hbase + (size_t)e * p.ff + 128 * j, tag, hv, abort_flag, gabort, p.err)) {
+                        break;
+                    }
+                    uint32_t bf[8][2];
+                    float inv;
+                    build_b(hv, bst, bf, inv);
+                    if (t + kNC < n_tasks) request(t + kNC);   // overlaps this task's decode
+                    if (!warp_wait_stage(&descs[s].seq, n, full0 + 8 * s, (n / kStages) & 1, p.err, abort_flag))
+                        break;
+                    const Desc d = descs[s];
+                    const int tl = e - d.a;
+                    const bool bad = (d.bad >> tl) & 1;
+                    float acc[2] = {0.f, 0.f};
+                    if (!bad)
+                        do_group_q(stages32 + s * kStageBytes + (uint32_t)tl * 16u * p.rb_dn, j, Ld, tab, bf, inv, acc);
+                    quad_sum(acc);
+                    if (c == 0) {
+                        dred[t * 16 + g] = bad ? nan : acc[0];
+                        dred[t * 16 + g + 8] = bad ? nan : acc[1];
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        // 16 arrivals per stage use: the stage's first task brings the missing ones
+                        const int first = d.a * p.Gd, in_stage = d.b * p.Gd;
+                        mbar_arrive_n(done0 + 8 * s, t == first ? 1u + (uint32_t)(kNC - in_stage) : 1u);
+                    }
                 }
-                float base;
-                if (L == 0)
-                    base = p.accumulate ? p.out[row] : 0.f;
-                else
-                    base = xown[r];
-                const float nv = base + tot;
-                __syncwarp();
-                if (lane < 16) {
-                    xown[r] = nv;   // next layer's base (read by this CTA's combine only)
-                    if (L + 1 < p.n_layers)
-                        st_pair(p.xpairs + (size_t)((L + 1) & 1) * p.d_model + row, nv, tag + 1u);
-                    else
-                        p.out[row] = nv;
-                }
-                __threadfence_block();
-                __syncwarp();
-                if (lane == 0) atomicExch(ucnt, 0);
             }
         }
     }
@@ -598,7 +521,7 @@ struct FlowScratch {
     bool stale = false;
 };
 FlowScratch g_fs;
-constexpr size_t kCtlBytes = 256;
+constexpr size_t kCtlBytes = 2048;   // words 0-2 used; bytes 256 .. 1279 read by the stall test, never written
 constexpr size_t kXPairBytes = 2 * 2048 * 8;
 constexpr size_t kHPairBytes = 2 * (size_t)kMaxUsed * 2048 * 8;
 constexpr int kMaxDev = 64;
@@ -680,7 +603,7 @@ int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
     p.d_model = a.d_model;
     p.ff = a.ff;
     p.n_gu_items = a.n_used * a.ff / 8;
-    p.tps = 2 * 16 * p.rb_dn <= kStageBytes ? 2 : 1;
+    p.tps = (2 * 16 * p.rb_dn <= kStageBytes && 2 * p.Gd <= kNC) ? 2 : 1;   // a stage's tasks <= 16
     p.n_dn_stages = (a.n_used + p.tps - 1) / p.tps;
     p.gu_stride = a.gu_expert_stride;
     p.dn_stride = a.down_expert_stride;
@@ -689,6 +612,10 @@ int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
     p.accumulate = a.accumulate;
     p.h = a.h;
     p.err = a.err;
+    {
+        const char* t = std::getenv("SABAH_TEST_FLOW_STALL");
+        p.stall_test = t && *t == '1';
+    }
     for (int L = 0; L < a.n_layers; ++L) {
         p.layer[L].gate = (const uint8_t*)a.gate_banks[L];
         p.layer[L].up = (const uint8_t*)a.up_banks[L];

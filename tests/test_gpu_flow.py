@@ -215,3 +215,35 @@ def test_bench_cfg2_token_all_layers(gpu_rt):
     del views, bank
     torch.cuda.empty_cache()
     assert r <= TOL and r <= TIGHT, r
+
+
+def test_flow_wait_that_never_ends_gives_up_and_recovers(gpu_rt):
+    """Failure detection without a GPU fault: with the test switch
+    SABAH_TEST_FLOW_STALL=1, one CTA first waits (short poll limit) for data
+    that nothing writes. The kernel must give up instead of hanging: every CTA
+    winds down, the device error word reads SB_DERR_TIMEOUT (2), and the next
+    call, without the switch, is clean and bit-identical to a normal run."""
+    d_model, ff, E, K, n_layers = 2048, 768, 64, 10, 3
+    banks = _banks(n_layers, E, d_model, ff, seed=4500)
+    rng = np.random.default_rng(45)
+    ids, w = _routing(rng, n_layers, E, K)
+    ids_d, w_d = torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda()
+    x0 = torch.randn((1, d_model), device="cuda")
+    h = torch.empty((1, K, ff), device="cuda")
+    from sabah_moe_accelerator_b200 import rt
+    x_ok = x0.clone()
+    rt.check(_decode(gpu_rt, banks, ids_d, w_d, x_ok, h, d_model, ff, E), "sabah_moe_decode")
+    torch.cuda.synchronize()
+    os.environ["SABAH_TEST_FLOW_STALL"] = "1"
+    try:
+        x = x0.clone()
+        rt.check(_decode(gpu_rt, banks, ids_d, w_d, x, h, d_model, ff, E), "sabah_moe_decode (stalled)")
+        torch.cuda.synchronize()   # returns: every wait is bounded
+    finally:
+        del os.environ["SABAH_TEST_FLOW_STALL"]
+    assert gpu_rt.sabah_rt_device_error() == 2
+    x = x0.clone()
+    rt.check(_decode(gpu_rt, banks, ids_d, w_d, x, h, d_model, ff, E), "sabah_moe_decode after the timeout")
+    torch.cuda.synchronize()
+    assert gpu_rt.sabah_rt_device_error() == 0
+    assert torch.equal(x, x_ok)

@@ -10,13 +10,14 @@ namespace sb_flow {
 
 using namespace sb_iq3s;
 
-// Grid-table format. 0: 4-byte entries (the grid bytes), 32 replicas, signs
+// Grid-table format (1 measured about 10% faster on B200 in the decode core
+// alone). 0: 4-byte entries (the grid bytes), 32 replicas, signs
 // placed by a multiply-spread and two PRMTs. 1: 8-byte entries holding the
 // entry already as two fp16-subnormal pairs, 16 replicas (a half-warp's
 // 8-byte loads hit distinct bank pairs), signs applied by two IMAD + LOP3.
 // Both tables are 64 KB: 128 bytes per entry across the replicas.
 #ifndef SB_FLOW_TABLE64
-#define SB_FLOW_TABLE64 0
+#define SB_FLOW_TABLE64 1
 #endif
 constexpr bool kTable64 = SB_FLOW_TABLE64 != 0;
 constexpr int kR = kTable64 ? 16 : 32;

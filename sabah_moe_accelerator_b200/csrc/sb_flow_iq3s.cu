@@ -60,6 +60,7 @@ constexpr int kMaxLayers = 64;               // tags hold the layer in 6 bits
 constexpr int kMaxUsed = 16;
 constexpr int kMaxDnTasks = 160;             // n_used * ff / 128
 constexpr long long kPollLimit = 1ll << 21;  // pair polls (~1 us each)
+constexpr int kMaxGrid = 192;                // CTAs (one per SM)
 
 struct Desc {
     int seq;    // sequence number of the stage's current contents
@@ -98,6 +99,10 @@ struct FlowParams {
     int rb_gu, rb_dn;          // row bytes
     int G, Gd;                 // 128-weight groups per gate/up row and per down row
     int n_gu_items;            // n_used * ff / 8
+    // gate/up items [gu_first[c], gu_first[c + 1]) belong to CTA c: chosen on the
+    // host so that every CTA's gate/up plus down work is about equal (the CTAs
+    // without a down unit take more gate/up items)
+    int gu_first[kMaxGrid + 1];
     int n_units;               // d_model / 16
     int tps;                   // down tiles per stage (1 or 2)
     int n_dn_stages;           // ceil(n_used / tps)
@@ -187,14 +192,7 @@ __device__ inline bool poll4(const unsigned long long* p, unsigned tag, float4& 
     return false;
 }
 
-// Gate/up items go round-robin over the CTAs in reverse order (item i to CTA
-// grid - 1 - i % grid), so the CTAs that get one item more than the rest
-// include those without a down unit (the units take CTAs 0 .. n_units - 1).
-__device__ inline int gu_rank(int cta) { return (int)gridDim.x - 1 - cta; }
-__device__ inline int gu_items_of(const FlowParams& p, int cta) {
-    const int r = gu_rank(cta);
-    return r < p.n_gu_items ? (p.n_gu_items - 1 - r) / (int)gridDim.x + 1 : 0;
-}
+__device__ inline int gu_items_of(const FlowParams& p, int cta) { return p.gu_first[cta + 1] - p.gu_first[cta]; }
 
 __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant__ FlowParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -243,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 int nt;
                 if (idx < ng) {
                     // stacked gate/up tile: 8 gate rows, then the same 8 up rows
-                    const int item = gu_rank(cta) + idx * (int)gridDim.x;
+                    const int item = p.gu_first[cta] + idx;
                     const int rpb = p.ff / 8;
                     d.a = item / rpb;
                     d.b = item % rpb;
@@ -580,7 +578,31 @@ int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
     }
     const int grid = g_flow_grid[dev];
     p.n_units = a.d_model / 16;
-    if (grid < p.n_units) return 0;   // every down unit needs a CTA of its own
+    if (grid < p.n_units || grid > kMaxGrid) return 0;   // every down unit needs a CTA of its own
+    // Gate/up items per CTA. A unit CTA also runs n_used * Gd down groups, a
+    // gate/up item is G groups: the CTAs without a unit take about that many
+    // more items (in groups), and every unit CTA the same count, so the down
+    // units, and with them the next layer's x rows, finish together. Items go
+    // in slot order: the unit CTAs take the first slots, whose h the down
+    // tasks (also in slot order) need first.
+    {
+        const int n_items = a.n_used * a.ff / 8, units = p.n_units, rest = grid - units;
+        const double extra = (double)(a.n_used * p.Gd) / p.G;   // a unit's down work, in items
+        int per_unit = (int)((n_items - rest * extra) / grid + 0.5);
+        per_unit = std::max(0, std::min(per_unit, n_items / units));
+        if (rest == 0) per_unit = n_items / grid;
+        int left = n_items - per_unit * units;
+        p.gu_first[0] = 0;
+        for (int c = 0; c < grid; ++c) {
+            int n;
+            if (rest > 0)
+                n = c < units ? per_unit : left / rest + ((c - units) < left % rest ? 1 : 0);
+            else
+                n = per_unit + (c < n_items - per_unit * grid ? 1 : 0);
+            p.gu_first[c + 1] = p.gu_first[c] + n;
+        }
+        if (p.gu_first[grid] != n_items) return 0;
+    }
 
     if (!g_fs.mem) {
         if (!sb_cuda_ok(cudaMalloc(&g_fs.mem, kCtlBytes + kXPairBytes + kHPairBytes), "flow scratch")) return -1;

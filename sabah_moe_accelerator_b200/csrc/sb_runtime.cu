@@ -38,6 +38,7 @@
 #include <vector>
 
 #include "sb_kernels.h"
+#include "sb_staging.h"
 #include "sb_quant.cuh"
 
 #define SABAH_API extern "C" __attribute__((visibility("default")))
@@ -197,17 +198,25 @@ struct Slab {
 Slab g_slab;
 
 // ---------------------------- residency -----------------------------------
+// Residency key: the host tensor's address (the reference's key), the expert,
+// its byte size and a tag of the tensor's shape (row stride, rows, k, type),
+// so a tensor of another shape met later at a reused address is a miss, not a
+// stale hit.
 struct Key {
     const void* src;
     int expert;
     size_t bytes;
-    bool operator==(const Key& o) const { return src == o.src && expert == o.expert && bytes == o.bytes; }
+    uint64_t shape;
+    bool operator==(const Key& o) const {
+        return src == o.src && expert == o.expert && bytes == o.bytes && shape == o.shape;
+    }
 };
 struct KeyHash {
     size_t operator()(const Key& k) const {
         uint64_t h = (uint64_t)(uintptr_t)k.src * 0x9E3779B97F4A7C15ull;
         h ^= (uint64_t)(uint32_t)k.expert + 0x632BE59BD9B4E019ull + (h << 6) + (h >> 2);
         h ^= (uint64_t)k.bytes * 0xBF58476D1CE4E5B9ull;
+        h ^= k.shape * 0x94D049BB133111EBull;
         return (size_t)h;
     }
 };
@@ -250,6 +259,7 @@ struct Fetch {
     void* dst;
     size_t bytes;
     int expert;
+    uint64_t shape;
 };
 
 void residency_reset_locked() {
@@ -329,9 +339,9 @@ void evict_until_locked(size_t need, std::set<uint64_t>& wait_epochs) {
 
 // Resident device copy of (src_key, expert): a hit, or a reserved slot recorded
 // in `miss` for the fill pass. nullptr on failure (message set).
-void* slot_locked(const void* src_key, int expert, const void* src, size_t bytes, std::vector<Fetch>& miss,
-                  std::set<uint64_t>& wait_epochs) {
-    const Key key{src_key, expert, bytes};
+void* slot_locked(const void* src_key, int expert, const void* src, size_t bytes, uint64_t shape,
+                  std::vector<Fetch>& miss, std::set<uint64_t>& wait_epochs) {
+    const Key key{src_key, expert, bytes, shape};
     auto it = g_res.map.find(key);
     if (it != g_res.map.end()) {
         Entry& e = it->second;
@@ -372,7 +382,7 @@ void* slot_locked(const void* src_key, int expert, const void* src, size_t bytes
     g_res.map.emplace(key, e);
     g_res.bytes += bytes;
     g_res.bytes_fetched += bytes;
-    miss.push_back({src, dev, bytes, expert});
+    miss.push_back({src, dev, bytes, expert, shape});
     return dev;
 }
 
@@ -384,12 +394,14 @@ bool fill_locked(const std::vector<Fetch>& miss, const std::set<uint64_t>& wait_
             !sb_cuda_ok(cudaStreamWaitEvent(g_rt.copy, g_res.done[r], 0), "copy stream wait"))
             return false;
     }
+    // pinned sources by direct DMA; pageable or file-mapped ones through the
+    // pinned staging ring and its reader lanes (sb_staging.cu)
+    std::vector<sb_fill> fills;
+    fills.reserve(miss.size());
+    for (const Fetch& f : miss) fills.push_back({f.dst, f.src, f.bytes});
+    if (!fills.empty() && !sb_stage_fill(fills.data(), (int)fills.size(), g_rt.copy)) return false;
     for (const Fetch& f : miss) {
-        if (!sb_cuda_ok(cudaMemcpyAsync(f.dst, f.src, f.bytes, cudaMemcpyHostToDevice, g_rt.copy), "expert H2D"))
-            return false;
-    }
-    for (const Fetch& f : miss) {
-        auto it = g_res.map.find(Key{src_key, f.expert, f.bytes});
+        auto it = g_res.map.find(Key{src_key, f.expert, f.bytes, f.shape});
         if (it != g_res.map.end()) it->second.filled = true;
         if (g_res.verify) {
             if (!sb_cuda_ok(cudaStreamSynchronize(g_rt.copy), "verify sync")) return false;
@@ -585,6 +597,8 @@ void selfcheck(const void* source, bool source_on_device, const sb_mmid_args& a,
 
 int snapshot_json(char* buf, size_t n) {
     std::lock_guard<std::mutex> l(g_res.mu);
+    sb_stage_stats ss{};
+    sb_stage_stats_get(&ss);
     char slots[256];
     int o = 0;
     for (int i = 0; i < 16; ++i)
@@ -596,7 +610,9 @@ int snapshot_json(char* buf, size_t n) {
         "\"overflow\":%llu,\"verify_ok\":%llu,\"verify_fail\":%llu,"
         "\"selfcheck_k\":%d,\"selfcheck_ok\":%llu,\"selfcheck_fail\":%llu,\"selfcheck_max_rel_l2\":%.6e,"
         "\"selfcheck_multi_token\":%llu,\"selfcheck_tensors\":%llu,\"selfcheck_slots\":[%s],"
-        "\"sentinel\":%d,\"device_calls\":%llu,\"id_reuse\":%llu}",
+        "\"sentinel\":%d,\"device_calls\":%llu,\"id_reuse\":%llu,"
+        "\"staged_bytes\":%llu,\"pinned_fill_bytes\":%llu,\"direct_io_reads\":%llu,\"direct_io_bytes\":%llu,"
+        "\"direct_io_fallbacks\":%llu,\"fill_waves\":%llu}",
         (unsigned long long)g_res.calls, (unsigned long long)g_res.empty_calls, (unsigned long long)g_res.tokens,
         (unsigned long long)(g_res.hits + g_res.misses), (unsigned long long)g_res.hits,
         (unsigned long long)g_res.misses, (unsigned long long)g_res.evictions,
@@ -605,7 +621,8 @@ int snapshot_json(char* buf, size_t n) {
         (unsigned long long)g_res.verify_fail, g_res.sc_k, (unsigned long long)g_res.sc_ok,
         (unsigned long long)g_res.sc_fail, g_res.sc_max, (unsigned long long)g_res.sc_multi_token,
         (unsigned long long)g_res.sc_tensors.size(), slots, SABAH_SENTINEL,
-        (unsigned long long)g_res.device_calls, (unsigned long long)g_res.id_reuse);
+        (unsigned long long)g_res.device_calls, (unsigned long long)g_res.id_reuse, ss.staged_bytes, ss.pinned_bytes,
+        ss.direct_io_reads, ss.direct_io_bytes, ss.direct_io_fallbacks, ss.waves);
 }
 
 void status_write() {
@@ -732,6 +749,7 @@ SABAH_API int sabah_rt_shutdown(void) {
         std::lock_guard<std::mutex> l(g_slab.mu);
         g_slab.destroy_locked();
     }
+    sb_stage_shutdown();
     scratch_destroy();
     pinned_destroy();
     if (g_rt.copy) cudaStreamDestroy(g_rt.copy);
@@ -1194,6 +1212,8 @@ SABAH_API int sabah_rt_mul_mat_id_v2(const void* source, size_t expert_stride, s
     std::vector<const void*> ptrs(n_slots);
     std::vector<Fetch> miss;
     std::set<uint64_t> wait_epochs;
+    const uint64_t shape = ((uint64_t)(uint32_t)qt << 56) ^ ((uint64_t)(uint32_t)rows << 32) ^
+                           ((uint64_t)(uint32_t)k << 8) ^ (uint64_t)row_stride * 0x9E3779B97F4A7C15ull;
     {
         std::lock_guard<std::mutex> l(g_res.mu);
         if (reuse) {
@@ -1212,7 +1232,7 @@ SABAH_API int sabah_rt_mul_mat_id_v2(const void* source, size_t expert_stride, s
                 if (i == 0) e = (e + 1) % n_experts;   // test-only build: neighbouring expert
 #endif
                 void* d = slot_locked(source, e, (const uint8_t*)source + (size_t)e * expert_stride, expert_stride,
-                                      miss, wait_epochs);
+                                      shape, miss, wait_epochs);
                 if (!d) return -1;
                 ptrs[(size_t)t * n_ids + i] = d;
             }

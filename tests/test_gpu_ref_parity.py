@@ -50,11 +50,18 @@ def _ref(mode, inputs, tmp_path, reps=0, env_extra=None):
     return d["out"], r.stderr
 
 
+# Host sources stay alive for the whole module: the hot tier is keyed by the
+# source address, as in the reference (a GGUF mapping lives as long as the
+# process), so a freed array's address must not come back as a new tensor.
+_SOURCES = []
+
+
 def _case(qt, rows, k, E, T, n_ids, seed):
     from sabah_moe_accelerator_b200 import ops, rt
     bank = ops.synth_rows(E * rows, k, qt, seed=seed, sigma=0.02)
     torch.cuda.synchronize()
     src = bank.cpu().numpy().reshape(E, rows * rt.row_bytes(qt, k))
+    _SOURCES.append(src)
     rng = np.random.default_rng(seed)
     ids = np.stack([rng.choice(E, n_ids, replace=False) for _ in range(T)]).astype(np.int32)
     x_rows = n_ids if rows > k else 1    # down: one input row per slot; gate/up: broadcast

@@ -1,0 +1,100 @@
+"""Hot-tier fill paths of the host-source MUL_MAT_ID (the llama.cpp contract):
+pageable memory and a file mapping go through the pinned staging ring (the
+file by O_DIRECT reads where the file system allows them), pinned memory by
+direct DMA (sabah/runtime/cuda/sabah_rt.cu:1033-1514, 2051-2116 in the
+reference). Every case must be byte-exact in the slab (verified against the
+source) and give the fp64 result.
+"""
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+TIGHT = 2e-5
+
+
+def _child(kind, tmp_path, env_extra=None):
+    env = dict(os.environ, SABAH_LLAMA_HOT_BYTES=str(1 << 30), SABAH_LLAMA_VERIFY_BYTES="1")
+    env.update(env_extra or {})
+    r = subprocess.run([sys.executable, "-c", _CHILD, kind, str(tmp_path)], cwd=ROOT, env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+@pytest.mark.parametrize("kind", ["pageable", "file", "pinned"])
+def test_fill_sources_are_exact(tmp_path, kind):
+    r = _child(kind, tmp_path)
+    assert r["rel"] <= TOL and r["rel"] <= TIGHT, r
+    s = r["snapshot"]
+    assert s["verify_fail"] == 0 and s["verify_ok"] > 0, s
+    assert s["misses"] > 0, s
+    if kind == "pinned":
+        assert s["pinned_fill_bytes"] > 0 and s["staged_bytes"] == 0, s
+    else:
+        assert s["staged_bytes"] >= s["bytes_fetched"] > 0 and s["pinned_fill_bytes"] == 0, s
+        assert s["fill_waves"] >= 1, s
+    if kind == "file":
+        # O_DIRECT where the file system supports it; a fallback to the mapping otherwise
+        assert s["direct_io_reads"] + s["direct_io_fallbacks"] > 0 or r["odirect_open"] is False, s
+    if kind == "pageable":
+        assert s["direct_io_reads"] == 0, s
+
+
+def test_file_fill_without_direct_io(tmp_path):
+    r = _child("file", tmp_path, {"SABAH_LLAMA_DIRECT_IO": "0"})
+    assert r["rel"] <= TIGHT, r
+    s = r["snapshot"]
+    assert s["direct_io_reads"] == 0 and s["staged_bytes"] > 0 and s["verify_fail"] == 0, s
+
+
+_CHILD = r"""
+import json, os, sys
+import numpy as np, torch
+sys.path.insert(0, os.getcwd())
+from oracle import cpu as orc
+from sabah_moe_accelerator_b200 import ops, rt
+kind, tmp = sys.argv[1], sys.argv[2]
+ops.init(0)
+qt, E, rows, k = 21, 64, 2048, 768       # IQ3_S down-shaped calls: one input row per slot
+rb = rt.row_bytes(qt, k)
+bank = ops.synth_rows(E * rows, k, qt, seed=123, sigma=0.02)
+torch.cuda.synchronize()
+host = bank.cpu().numpy()
+odirect_open = None
+if kind == "pageable":
+    src = host.copy()
+elif kind == "pinned":
+    pin = torch.empty(host.size, dtype=torch.uint8).pin_memory()
+    pin.numpy()[:] = host
+    src = pin.numpy()
+else:
+    path = os.path.join(tmp, "bank.bin")
+    host.tofile(path)
+    src = np.memmap(path, dtype=np.uint8, mode="r")
+    try:
+        fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+        os.close(fd)
+        odirect_open = True
+    except OSError:
+        odirect_open = False
+rng = np.random.default_rng(5)
+T, K = 3, 10
+ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+x = (rng.standard_normal((T, K, k)) * 0.1).astype(np.float32)
+out = ops.mul_mat_id(src, rows * rb, rb, torch.from_numpy(x).cuda(), torch.from_numpy(ids).cuda(), rows, k, E, qt)
+torch.cuda.synchronize()
+exact = orc.mmid_f64(host, rows * rb, rb, x, K, ids, rows, k, E, qt)
+print(json.dumps(dict(rel=orc.rel_l2(out.cpu().numpy(), exact), snapshot=rt.snapshot(), odirect_open=odirect_open)))
+"""

@@ -72,49 +72,49 @@ __device__ inline void decode_entry(uint32_t qs, uint32_t qh, uint32_t sbyte, ui
     }
 }
 
-// B fragments of mma.sync m16n8k16 for one 128-element group of a vector, lane
-// l holding elements [4l, 4l + 4): per sub-block (8 lanes) a power-of-two
-// scale puts the max into [2^13, 2^14); each value splits into fp16 hi and lo.
-// Lane (g, c) gets, for step S, the hi (g even) or lo (g odd) pairs of entry S
-// of sub-block c when g / 2 == c, zeros otherwise (the K permutation of the
-// decode core), and inv = 2^24 / scale of sub-block c.
-__device__ inline void build_b(float4 v4, uint32_t bst, uint32_t (&bf)[8][2], float& inv) {
+// B operand of mma.sync m16n8k16 for one 128-element group of a vector, lane
+// l holding elements [4l, 4l + 4). One power-of-two scale for the group puts
+// its max into [2^13, 2^14) (a warp max reduction, REDUX); each value splits
+// into fp16 hi and lo parts, which keep about 22 bits of it. stage_b writes
+// lane l's (hi01, hi23, lo01, lo23) to the warp's 512-byte staging area and
+// returns 2^24 / scale (the 2^24 undoes the subnormal encoding of the weights).
+__device__ inline float stage_b(float4 v4, uint32_t bst) {
     const int lane = threadIdx.x & 31;
-    float m = fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w)));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-    int ex = 0;
-    if (m > 0.f && isfinite(m)) {
-        frexpf(m, &ex);   // m = f * 2^ex, f in [0.5, 1)
-        ex = max(-100, min(100, 14 - ex));
-    }
-    const float s = ldexpf(1.f, ex);
-    const float v[4] = {v4.x * s, v4.y * s, v4.z * s, v4.w * s};
-    __half hi[4], lo[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        hi[i] = __float2half_rn(v[i]);
-        lo[i] = __float2half_rn(v[i] - __half2float(hi[i]));
-    }
-    const __half2 h01 = __halves2half2(hi[0], hi[1]), h23 = __halves2half2(hi[2], hi[3]);
-    const __half2 l01 = __halves2half2(lo[0], lo[1]), l23 = __halves2half2(lo[2], lo[3]);
+    const float m = fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w)));
+    // positive floats order as their bit patterns; NaN and inf give no scaling
+    const unsigned mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+    const int E = (int)(mb >> 23);   // biased exponent of the max: max = f * 2^(E - 126), f in [0.5, 1)
+    const int ex = (mb == 0u || E == 255) ? 0 : max(-100, min(100, 14 - (E - 126)));
+    const float s = __int_as_float((ex + 127) << 23);
+    const float2 a = make_float2(v4.x * s, v4.y * s), b = make_float2(v4.z * s, v4.w * s);
+    const __half2 h01 = __float22half2_rn(a), h23 = __float22half2_rn(b);
+    const float2 ra = __half22float2(h01), rb = __half22float2(h23);
+    const __half2 l01 = __float22half2_rn(make_float2(a.x - ra.x, a.y - ra.y));
+    const __half2 l23 = __float22half2_rn(make_float2(b.x - rb.x, b.y - rb.y));
     asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(bst + 16u * lane), "r"(*(const uint32_t*)&h01),
                  "r"(*(const uint32_t*)&h23), "r"(*(const uint32_t*)&l01), "r"(*(const uint32_t*)&l23)
                  : "memory");
-    const float my_inv = 16777216.0f / s;   // 2^24 undoes the subnormal encoding of the weights
+    return __int_as_float((24 - ex + 127) << 23);
+}
+
+// Lane (g, c)'s B fragment of step S from a staged group: the hi (g even) or
+// lo (g odd) pairs of entry S of sub-block c when g / 2 == c, zeros otherwise
+// (the K permutation of the decode core).
+__device__ inline void load_b(uint32_t bst, int S, uint32_t& b0, uint32_t& b1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    b0 = b1 = 0;
+    if ((g >> 1) == c)
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1)
+                     : "r"(bst + 16u * (8 * c + S) + 8u * (g & 1)));
+}
+
+// B fragments of all 8 steps in registers (the gate/up path keeps them for
+// every item of a layer).
+__device__ inline void build_b(float4 v4, uint32_t bst, uint32_t (&bf)[8][2], float& inv) {
+    inv = stage_b(v4, bst);
     __syncwarp();
-    const int g = lane >> 2, c = lane & 3;
-    inv = __shfl_sync(0xffffffffu, my_inv, 8 * c);
-    const bool mine = (g >> 1) == c;
-    const uint32_t src = bst + 16u * (8 * c) + 8u * (g & 1);
 #pragma unroll
-    for (int S = 0; S < 8; ++S) {
-        uint32_t b0 = 0, b1 = 0;
-        if (mine) asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(src + 16u * S));
-        bf[S][0] = b0;
-        bf[S][1] = b1;
-    }
+    for (int S = 0; S < 8; ++S) load_b(bst, S, bf[S][0], bf[S][1]);
     __syncwarp();   // the staging area may be rewritten after this
 }
 
@@ -236,6 +236,44 @@ __device__ inline void do_group2_q(uint32_t tile0, uint32_t tile1, int q, const 
         do_group2<1>(tile0 + o, tile1 + o, L, tab, bf, inv, acc0, acc1);
     else
         do_group2<0>(tile0 + o, tile1 + o, L, tab, bf, inv, acc0, acc1);
+}
+
+// Both groups (sub-blocks 0-3 and 4-7) of the super-block at sb of one
+// 16-row tile, with each group's B staged in shared memory (bst0, bst1) and
+// its own scale: two independent MMA chains; acc gets rows g and g + 8.
+template <int S>
+__device__ inline void step_sb(uint32_t table, const uint32_t (&qsw)[2][2][4], const uint32_t (&QH)[2][2][2],
+                               const uint32_t (&sgw)[2][2][4], uint32_t bst0, uint32_t bst1, float (&dd)[2][4]) {
+    uint32_t a[2][2][2];
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            decode_entry<S>(qsw[n][h][S >> 1], QH[n][h][S >> 2], sgw[n][h][S >> 1], table, a[n][h][0], a[n][h][1]);
+    uint32_t b[2][2];
+    load_b(bst0, S, b[0][0], b[0][1]);
+    load_b(bst1, S, b[1][0], b[1][1]);
+#pragma unroll
+    for (int n = 0; n < 2; ++n) mma16816(dd[n], a[n][0][0], a[n][1][0], a[n][0][1], a[n][1][1], b[n][0], b[n][1]);
+}
+
+__device__ inline void do_superblock(uint32_t sb, const Lane& L, uint32_t tab, uint32_t bst0, float inv0, uint32_t bst1,
+                                     float inv1, float (&acc)[2]) {
+    uint32_t qsw[2][2][4], QH[2][2][2], sgw[2][2][4];
+    float db[2][2];
+    fields<0>(sb, L, inv0, qsw[0], QH[0], sgw[0], db[0]);
+    fields<1>(sb, L, inv1, qsw[1], QH[1], sgw[1], db[1]);
+    float dd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    step_sb<0>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    step_sb<1>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    step_sb<2>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    step_sb<3>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    step_sb<4>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    step_sb<5>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    step_sb<6>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    step_sb<7>(tab, qsw, QH, sgw, bst0, bst1, dd);
+    acc[0] = fmaf(db[0][0], dd[0][0] + dd[0][1], db[1][0] * (dd[1][0] + dd[1][1]));
+    acc[1] = fmaf(db[0][1], dd[0][2] + dd[0][3], db[1][1] * (dd[1][2] + dd[1][3]));
 }
 
 // rows g, g + 8 of the quad's partial sums, summed over the quad (c = 0..3)

@@ -58,9 +58,13 @@ constexpr int kStageBytes = 16 * 880;        // a stacked gate/up tile at d_mode
 constexpr int kStages = 9;                   // = issuing producer lanes: lane l owns stage l
 constexpr int kMaxLayers = 64;               // tags hold the layer in 6 bits
 constexpr int kMaxUsed = 16;
-constexpr int kMaxDnTasks = 160;             // n_used * ff / 128
+constexpr int kMaxDnTasks = 128;             // down tasks (slot, super-block): n_used * ff / 256
 constexpr long long kPollLimit = 1ll << 21;  // pair polls (~1 us each)
 constexpr int kMaxGrid = 192;                // CTAs (one per SM)
+// mbarrier waits here use a short suspend-time hint: with the 20 us hint of the
+// other kernels, warps waiting on a stage whose bulk copy had landed were
+// measured (globaltimer trace) to resume up to ~15 us late
+constexpr int kHintNs = 200;
 
 struct Desc {
     int seq;    // sequence number of the stage's current contents
@@ -76,8 +80,8 @@ struct Smem {
     static constexpr int stages = table + kGridBytes;
     static constexpr int red = stages + kStages * kStageBytes;          // [kStages][kNC][16] float
     static constexpr int dred = red + kStages * kNC * 16 * 4;          // [kMaxDnTasks][16] float
-    static constexpr int bst = dred + kMaxDnTasks * 16 * 4;            // [kNC][32][16 B] B staging
-    static constexpr int desc = bst + kNC * 512;                       // [kStages] Desc
+    static constexpr int bst = dred + kMaxDnTasks * 16 * 4;            // [kNC][2 groups][32][16 B] B staging
+    static constexpr int desc = bst + kNC * 1024;                      // [kStages] Desc
     static constexpr int abort_flag = desc + kStages * (int)sizeof(Desc);
     static constexpr int bars = (abort_flag + 4 + 7) & ~7;             // full, empty, done [kStages] each
     static constexpr int total = bars + 3 * kStages * 8;
@@ -119,6 +123,7 @@ struct FlowParams {
     // limit, for pairs that nothing writes, so the kernel must give up, record
     // SB_DERR_TIMEOUT and return; the next call runs clean
     int stall_test;
+    int l2_prefetch;   // producer lanes warm L2 with their next tiles (SABAH_IQ3S_FLOW_L2=1; measured slower, off)
     FlowLayer layer[kMaxLayers];
 };
 
@@ -165,7 +170,7 @@ __device__ inline bool warp_aborting(volatile int* abort_flag, const unsigned* g
 __device__ inline bool warp_wait_stage(const int* stamp, int seq, uint32_t full, uint32_t parity, int* err,
                                        volatile int* abort_flag) {
     const bool stamped = __all_sync(0xffffffffu, wait_seq(stamp, seq, err, abort_flag));
-    return stamped && __all_sync(0xffffffffu, mbar_wait(full, parity, err, abort_flag));
+    return stamped && __all_sync(0xffffffffu, mbar_wait<kHintNs>(full, parity, err, abort_flag));
 }
 
 // Warp-cooperative: lane l reads pairs [4l, 4l + 4) at p and returns their
@@ -192,7 +197,76 @@ __device__ inline bool poll4(const unsigned long long* p, unsigned tag, float4& 
     return false;
 }
 
+// Lane l's 8 pairs of a 256-value piece of h at q: pairs [4l, 4l + 4) of each
+// 128-value half, requested now and checked later
+__device__ inline void request_pairs(const unsigned long long* q, unsigned long long (&pv)[8]) {
+    q += 4 * (threadIdx.x & 31);
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[0]), "=l"(pv[1]) : "l"(q) : "memory");
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[2]), "=l"(pv[3]) : "l"(q + 2) : "memory");
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[4]), "=l"(pv[5]) : "l"(q + 128) : "memory");
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[6]), "=l"(pv[7]) : "l"(q + 130) : "memory");
+}
+
 __device__ inline int gu_items_of(const FlowParams& p, int cta) { return p.gu_first[cta + 1] - p.gu_first[cta]; }
+
+// The tiles of this CTA's sequence number n: gate/up items (a stacked tile: 8
+// gate rows, then the same 8 up rows) and down stages (16 rows of the CTA's
+// unit for up to tps consecutive slots). Fills the descriptor (bad tiles get
+// their bit and no source) and the copies: source, bytes, offset in the stage.
+struct Tiles {
+    const uint8_t* src[2];
+    uint32_t bytes[2], off[2];
+    int n;
+};
+__device__ inline Tiles stage_tiles(const FlowParams& p, int cta, int n, int per, int ng, Desc& d) {
+    const int L = n / per, idx = n % per;
+    const FlowLayer& lb = p.layer[L];
+    Tiles t{};
+    d.bad = 0;
+    if (idx < ng) {
+        const int item = p.gu_first[cta] + idx;
+        const int rpb = p.ff / 8;
+        d.a = item / rpb;
+        d.b = item % rpb;
+        int id = lb.ids[d.a];
+#if SABAH_SENTINEL == 1
+        if (d.a == 0 && id >= 0 && id < p.n_experts) id = (id + 1) % p.n_experts;   // test-only build
+#endif
+        t.n = 2;
+        if (id < 0 || id >= p.n_experts) {
+            d.bad = 1;
+        } else {
+            const size_t o = (size_t)id * p.gu_stride + (size_t)d.b * 8 * p.rb_gu;
+            t.src[0] = lb.gate + o;
+            t.src[1] = lb.up + o;
+            t.bytes[0] = t.bytes[1] = 8u * p.rb_gu;
+            t.off[1] = 8u * p.rb_gu;
+        }
+    } else {
+        const int ds = idx - ng;
+        d.a = ds * p.tps;
+        d.b = min(p.tps, p.n_used - d.a);
+        t.n = d.b;
+        for (int k = 0; k < t.n; ++k) {
+            int id = lb.ids[d.a + k];
+#if SABAH_SENTINEL == 1
+            if (d.a + k == 0 && id >= 0 && id < p.n_experts) id = (id + 1) % p.n_experts;
+#endif
+            if (id < 0 || id >= p.n_experts) {
+                d.bad |= 1 << k;
+            } else {
+                t.src[k] = lb.down + (size_t)id * p.dn_stride + (size_t)cta * 16 * p.rb_dn;
+                t.bytes[k] = 16u * p.rb_dn;
+                t.off[k] = (uint32_t)k * 16u * p.rb_dn;
+            }
+        }
+    }
+    return t;
+}
+
+__device__ inline void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
 __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant__ FlowParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -231,72 +305,36 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
             for (int n = lane; n < total; n += kStages) {
                 if (aborting(abort_flag, gabort)) break;
                 const int s = n % kStages;
-                if (n >= kStages && !mbar_wait(empty0 + 8 * s, ((n / kStages) - 1) & 1, p.err, abort_flag)) break;
-                const int L = n / per, idx = n % per;
-                const FlowLayer& lb = p.layer[L];
+                if (n >= kStages && !mbar_wait<kHintNs>(empty0 + 8 * s, ((n / kStages) - 1) & 1, p.err, abort_flag)) break;
                 Desc d;
-                d.bad = 0;
-                const uint8_t* src[2] = {nullptr, nullptr};
-                uint32_t bytes[2] = {0, 0}, off[2] = {0, 0};
-                int nt;
-                if (idx < ng) {
-                    // stacked gate/up tile: 8 gate rows, then the same 8 up rows
-                    const int item = p.gu_first[cta] + idx;
-                    const int rpb = p.ff / 8;
-                    d.a = item / rpb;
-                    d.b = item % rpb;
-                    int id = lb.ids[d.a];
-#if SABAH_SENTINEL == 1
-                    if (d.a == 0 && id >= 0 && id < p.n_experts) id = (id + 1) % p.n_experts;   // test-only build
-#endif
-                    nt = 2;
-                    if (id < 0 || id >= p.n_experts) {
-                        d.bad = 1;
-                    } else {
-                        const size_t o = (size_t)id * p.gu_stride + (size_t)d.b * 8 * p.rb_gu;
-                        src[0] = lb.gate + o;
-                        src[1] = lb.up + o;
-                        bytes[0] = bytes[1] = 8u * p.rb_gu;
-                        off[1] = 8u * p.rb_gu;
-                    }
-                } else {
-                    // down tiles: 16 rows of this CTA's unit for tps consecutive slots
-                    const int ds = idx - ng;
-                    d.a = ds * p.tps;
-                    d.b = min(p.tps, p.n_used - d.a);
-                    nt = d.b;
-                    for (int t = 0; t < nt; ++t) {
-                        int id = lb.ids[d.a + t];
-#if SABAH_SENTINEL == 1
-                        if (d.a + t == 0 && id >= 0 && id < p.n_experts) id = (id + 1) % p.n_experts;
-#endif
-                        if (id < 0 || id >= p.n_experts) {
-                            d.bad |= 1 << t;
-                        } else {
-                            src[t] = lb.down + (size_t)id * p.dn_stride + (size_t)cta * 16 * p.rb_dn;
-                            bytes[t] = 16u * p.rb_dn;
-                            off[t] = (uint32_t)t * 16u * p.rb_dn;
-                        }
-                    }
-                }
+                const Tiles t = stage_tiles(p, cta, n, per, ng, d);
                 d.seq = -1;
                 descs[s] = d;
                 __threadfence_block();
                 *(volatile int*)&descs[s].seq = n;   // the stage's previous use is released
                 uint32_t tot = 0;
-                for (int t = 0; t < nt; ++t) tot += bytes[t];
+                for (int k = 0; k < t.n; ++k) tot += t.bytes[k];
                 if (tot) {
                     mbar_expect_tx(full0 + 8 * s, tot);
-                    for (int t = 0; t < nt; ++t)
-                        if (bytes[t]) bulk_g2s(st0 + s * kStageBytes + off[t], src[t], bytes[t], full0 + 8 * s);
+                    for (int k = 0; k < t.n; ++k)
+                        if (t.bytes[k]) bulk_g2s(st0 + s * kStageBytes + t.off[k], t.src[k], t.bytes[k], full0 + 8 * s);
                 } else {
                     mbar_arrive(full0 + 8 * s);
                 }
                 last = n;
+                // while this lane waits for its stage to come free again, its next
+                // tiles are already on their way into L2: the copy then hits L2
+                if (p.l2_prefetch && n + kStages < total) {
+                    Desc dn;
+                    const Tiles tn = stage_tiles(p, cta, n + kStages, per, ng, dn);
+                    for (int k = 0; k < tn.n; ++k)
+                        if (tn.bytes[k]) prefetch_l2(tn.src[k], tn.bytes[k]);
+                }
             }
             // never leave with a copy in flight: the last use of this lane's stage must have landed
             if (last >= 0)
-                for (long long i = 0; i < kSpinLimit && !mbar_try_wait(full0 + 8 * (last % kStages),
+                for (long long i = 0; i < kSpinLimit * (kSuspendNs / kHintNs) &&
+                                    !mbar_try_wait<kHintNs>(full0 + 8 * (last % kStages),
                                                                        (last / kStages) & 1); ++i) {
                 }
         }
@@ -306,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
     float* red = (float*)(smem + Smem::red);
     float* dred = (float*)(smem + Smem::dred);
     const unsigned epoch = ld_relaxed_u32(p.ctl);
-    const int n_tasks = p.n_used * p.Gd;
+    const int n_tasks = p.n_used * p.Gd / 2;   // down tasks per unit: (slot, super-block)
     const float nan = __int_as_float(0x7fc00000);
 
     if (warp == kEpilogue) {
@@ -324,9 +362,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
         for (int L = 0; L < p.n_layers && ok; ++L) {
             const unsigned tag = (epoch << 6) + (unsigned)L + 1u;
             const FlowLayer& lb = p.layer[L];
+            // the layer's routing weights, lane e holding w[e], loaded before any wait
+            const float wl = lane < p.n_used ? __ldg(lb.w + lane) : 0.f;
             for (int k = 0; k < per && ok; ++k) {
                 const int n = L * per + k, s = n % kStages;
-                ok = __all_sync(0xffffffffu, mbar_wait(done0 + 8 * s, (n / kStages) & 1, p.err, abort_flag));
+                ok = __all_sync(0xffffffffu, mbar_wait<kHintNs>(done0 + 8 * s, (n / kStages) & 1, p.err, abort_flag));
                 if (!ok) break;
                 const Desc d = descs[s];
                 if (k < ng) {
@@ -353,12 +393,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 }
             }
             if (!ok || nd == 0) continue;
-            // every task of the unit is done: groups in order, slots in order (weighted)
+            // every task of the unit is done: super-blocks in order, slots in order (weighted)
+            const int spr = p.Gd / 2;
             float tot = 0.f;
             for (int e2 = 0; e2 < p.n_used; ++e2) {
                 float v = 0.f;
-                for (int j2 = 0; j2 < p.Gd; ++j2) v += dred[(e2 * p.Gd + j2) * 16 + r];
-                tot += __ldg(lb.w + e2) * v;
+                for (int j2 = 0; j2 < spr; ++j2) v += dred[(e2 * spr + j2) * 16 + r];
+                tot += __shfl_sync(0xffffffffu, wl, e2) * v;
             }
             xr = xr + tot;
             __syncwarp();   // dred is read before the next layer's tasks may write it
@@ -379,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
         const Lane Lg = lane_init<kR>(table, p.rb_gu, lane);
         const Lane Ld = lane_init<kR>(table, p.rb_dn, lane);
         const uint32_t stages32 = smem_u32(smem + Smem::stages);
-        const uint32_t bst = smem_u32(smem + Smem::bst) + 512u * warp;
+        const uint32_t bst = smem_u32(smem + Smem::bst) + 1024u * warp;
         // warp 0 supplies the arrivals of the gate/up warps that do not exist (G < 16)
         const uint32_t gu_arrivals = warp == 0 ? 1u + (uint32_t)(kNC - p.G) : 1u;
 
@@ -442,38 +483,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                     }
                 }
             }
-            // -------------------------------------------- down: tasks (slot, group) of this CTA's unit
+            // -------------------------------------------- down: tasks (slot, super-block) of this CTA's unit
             if (nd > 0 && warp < n_tasks) {
+                const int spr = p.Gd / 2;   // super-blocks per down row
                 const unsigned long long* hbase = p.hpairs + (size_t)(L & 1) * p.n_used * p.ff;
-                // the first task's pairs are requested before anything waits on them
-                unsigned long long pv[4];
-                auto request = [&](int t) {
-                    const unsigned long long* q =
-                        hbase + (size_t)(t / p.Gd) * p.ff + 128 * (t % p.Gd) + 4 * lane;
-                    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[0]), "=l"(pv[1]) : "l"(q)
-                                 : "memory");
-                    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[2]), "=l"(pv[3])
-                                 : "l"(q + 2)
-                                 : "memory");
-                };
-                request(warp);
+                // a task's 256 values of h (two 128-value pieces) are requested
+                // before anything waits on them, the next task's during this one
+                unsigned long long pv[8];
+                request_pairs(hbase + (size_t)(warp / spr) * p.ff + 256 * (warp % spr), pv);
                 for (int t = warp; t < n_tasks; t += kNC) {
-                    const int e = t / p.Gd, j = t % p.Gd;
+                    const int e = t / spr, sb = t % spr;
                     const int ds = e / p.tps, n = seq0 + ng + ds, s = n % kStages;
-                    // the requested pairs, if they already carry this layer's tag; else poll
-                    float4 hv;
-                    const bool ready = (unsigned)(pv[0] >> 32) == tag && (unsigned)(pv[1] >> 32) == tag &&
-                                       (unsigned)(pv[2] >> 32) == tag && (unsigned)(pv[3] >> 32) == tag;
+                    float4 hv[2];
+                    bool ready = true;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) ready = ready && (unsigned)(pv[k] >> 32) == tag;
                     if (__all_sync(0xffffffffu, ready)) {
-                        hv = make_float4(__uint_as_float((unsigned)pv[0]), __uint_as_float((unsigned)pv[1]),
-                                         __uint_as_float((unsigned)pv[2]), __uint_as_float((unsigned)pv[3]));
-                    } else if (!poll4(hbase + (size_t)e * p.ff + 128 * j, tag, hv, abort_flag, gabort, p.err)) {
+#pragma unroll
+                        for (int k = 0; k < 2; ++k)
+                            hv[k] = make_float4(__uint_as_float((unsigned)pv[4 * k]), __uint_as_float((unsigned)pv[4 * k + 1]),
+                                                __uint_as_float((unsigned)pv[4 * k + 2]),
+                                                __uint_as_float((unsigned)pv[4 * k + 3]));
+                    } else if (!poll4(hbase + (size_t)e * p.ff + 256 * sb, tag, hv[0], abort_flag, gabort, p.err) ||
+                               !poll4(hbase + (size_t)e * p.ff + 256 * sb + 128, tag, hv[1], abort_flag, gabort, p.err)) {
                         break;
                     }
-                    uint32_t bf[8][2];
-                    float inv;
-                    build_b(hv, bst, bf, inv);
-                    if (t + kNC < n_tasks) request(t + kNC);   // overlaps this task's decode
+                    const float inv0 = stage_b(hv[0], bst), inv1 = stage_b(hv[1], bst + 512u);
+                    __syncwarp();
+                    if (t + kNC < n_tasks)   // overlaps this task's decode
+                        request_pairs(hbase + (size_t)((t + kNC) / spr) * p.ff + 256 * ((t + kNC) % spr), pv);
                     if (!warp_wait_stage(&descs[s].seq, n, full0 + 8 * s, (n / kStages) & 1, p.err, abort_flag))
                         break;
                     const Desc d = descs[s];
@@ -481,16 +519,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                     const bool bad = (d.bad >> tl) & 1;
                     float acc[2] = {0.f, 0.f};
                     if (!bad)
-                        do_group_q(stages32 + s * kStageBytes + (uint32_t)tl * 16u * p.rb_dn, j, Ld, tab, bf, inv, acc);
+                        do_superblock(stages32 + s * kStageBytes + (uint32_t)tl * 16u * p.rb_dn + (uint32_t)sb * 110u, Ld,
+                                      tab, bst, inv0, bst + 512u, inv1, acc);
                     quad_sum(acc);
                     if (c == 0) {
                         dred[t * 16 + g] = bad ? nan : acc[0];
                         dred[t * 16 + g + 8] = bad ? nan : acc[1];
                     }
-                    __syncwarp();
+                    __syncwarp();   // the staging area is read; dred is written
                     if (lane == 0) {
                         // 16 arrivals per stage use: the stage's first task brings the missing ones
-                        const int first = d.a * p.Gd, in_stage = d.b * p.Gd;
+                        const int first = d.a * spr, in_stage = d.b * spr;
                         mbar_arrive_n(done0 + 8 * s, t == first ? 1u + (uint32_t)(kNC - in_stage) : 1u);
                     }
                 }
@@ -556,7 +595,7 @@ int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
     if (16 * p.rb_gu > kStageBytes || 16 * p.rb_dn > kStageBytes || (8 * p.rb_gu) % 16) return 0;
     p.G = a.d_model / 128;
     p.Gd = a.ff / 128;
-    if (a.n_used * p.Gd > kMaxDnTasks) return 0;
+    if (a.n_used * p.Gd / 2 > kMaxDnTasks) return 0;
     for (int L = 0; L < a.n_layers; ++L)
         for (const void* b : {a.gate_banks[L], a.up_banks[L], a.down_banks[L]})
             if (!b || !a16(b)) return 0;
@@ -625,7 +664,7 @@ int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
     p.d_model = a.d_model;
     p.ff = a.ff;
     p.n_gu_items = a.n_used * a.ff / 8;
-    p.tps = (2 * 16 * p.rb_dn <= kStageBytes && 2 * p.Gd <= kNC) ? 2 : 1;   // a stage's tasks <= 16
+    p.tps = (2 * 16 * p.rb_dn <= kStageBytes && p.Gd <= kNC) ? 2 : 1;   // a stage's tasks (tps * Gd / 2) <= 16
     p.n_dn_stages = (a.n_used + p.tps - 1) / p.tps;
     p.gu_stride = a.gu_expert_stride;
     p.dn_stride = a.down_expert_stride;
@@ -637,6 +676,8 @@ int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
     {
         const char* t = std::getenv("SABAH_TEST_FLOW_STALL");
         p.stall_test = t && *t == '1';
+        const char* l2 = std::getenv("SABAH_IQ3S_FLOW_L2");
+        p.l2_prefetch = l2 && *l2 == '1';
     }
     for (int L = 0; L < a.n_layers; ++L) {
         p.layer[L].gate = (const uint8_t*)a.gate_banks[L];

@@ -44,21 +44,24 @@ __device__ inline void mbar_arrive(uint32_t bar) {
 // try_wait with a suspend-time hint: a thread whose phase is not complete
 // sleeps (up to the hint) instead of spinning, so waiting producer lanes and
 // consumers do not steal issue slots from the warps that are decoding
+template <int HINT_NS = kSuspendNs>
 __device__ inline bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "n"(kSuspendNs)
+        : "r"(bar), "r"(parity), "n"(HINT_NS)
         : "memory");
     return ok != 0;
 }
 // Bounded wait. False when the CTA is aborting or when this wait gives up (it
 // then sets the abort flag and the device error word). Callers skip their work
 // but keep taking part in every barrier, so nothing is left waiting.
+template <int HINT_NS = kSuspendNs>
 __device__ inline bool mbar_wait(uint32_t bar, uint32_t parity, int* err, volatile int* abort_flag) {
-    for (long long i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+    const long long limit = kSpinLimit * (kSuspendNs / HINT_NS);   // the same ~2.6 s bound for any hint
+    for (long long i = 0; i < limit; ++i) {
+        if (mbar_try_wait<HINT_NS>(bar, parity)) return true;
         if ((i & 15) == 15 && *abort_flag) return false;
     }
     *abort_flag = 1;

@@ -40,6 +40,7 @@
 // that gives up records SB_DERR_TIMEOUT, raises a global abort word that the
 // other CTAs' polls read, skips its remaining work and drains its copies.
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 
@@ -61,10 +62,15 @@ constexpr int kMaxUsed = 16;
 constexpr int kMaxDnTasks = 128;             // down tasks (slot, super-block): n_used * ff / 256
 constexpr long long kPollLimit = 1ll << 21;  // pair polls (~1 us each)
 constexpr int kMaxGrid = 192;                // CTAs (one per SM)
+constexpr int kMaxRounds = 64;               // gate/up items of one CTA per layer
 // mbarrier waits here use a short suspend-time hint: with the 20 us hint of the
 // other kernels, warps waiting on a stage whose bulk copy had landed were
 // measured (globaltimer trace) to resume up to ~15 us late
 constexpr int kHintNs = 200;
+// Gate/up partial rows are stored row-major so that the epilogue reads a
+// row's 16 warp partials with 16-byte loads; the padded stride keeps 8
+// consecutive rows on 8 distinct 4-bank groups (conflict-free accesses)
+constexpr int kRedStride = kNC + 4;
 
 struct Desc {
     int seq;    // sequence number of the stage's current contents
@@ -78,8 +84,8 @@ struct Desc {
 struct Smem {
     static constexpr int table = 0;
     static constexpr int stages = table + kGridBytes;
-    static constexpr int red = stages + kStages * kStageBytes;          // [kStages][kNC][16] float
-    static constexpr int dred = red + kStages * kNC * 16 * 4;          // [kMaxDnTasks][16] float
+    static constexpr int red = stages + kStages * kStageBytes;          // [kStages][16 rows][kRedStride] float
+    static constexpr int dred = red + kStages * 16 * kRedStride * 4;   // [kMaxDnTasks][16 rows] float
     static constexpr int bst = dred + kMaxDnTasks * 16 * 4;            // [kNC][2 groups][32][16 B] B staging
     static constexpr int desc = bst + kNC * 1024;                      // [kStages] Desc
     static constexpr int abort_flag = desc + kStages * (int)sizeof(Desc);
@@ -88,7 +94,7 @@ struct Smem {
 };
 static_assert(Smem::total <= 227 * 1024, "shared memory budget");
 static_assert(Smem::stages % 128 == 0 && kStageBytes % 128 == 0, "stage alignment");
-static_assert(Smem::bst % 16 == 0, "B staging alignment");
+static_assert(Smem::bst % 16 == 0 && Smem::red % 16 == 0, "16-byte rows");
 
 struct FlowLayer {
     const uint8_t* gate;
@@ -103,11 +109,16 @@ struct FlowParams {
     int rb_gu, rb_dn;          // row bytes
     int G, Gd;                 // 128-weight groups per gate/up row and per down row
     int n_gu_items;            // n_used * ff / 8
-    // gate/up items [gu_first[c], gu_first[c + 1]) belong to CTA c: chosen on the
-    // host so that every CTA's gate/up plus down work is about equal (the CTAs
-    // without a down unit take more gate/up items)
-    int gu_first[kMaxGrid + 1];
-    int n_units;               // d_model / 16
+    int n_units;               // d_model / 16: CTAs [0, n_units) each own a down unit
+    // Gate/up items per CTA: pu (+1 for CTAs below urem) on a unit CTA, pn (+1
+    // for the first prem others) elsewhere, chosen on the host so that a unit
+    // CTA's gate/up plus down work matches the others' gate/up work. Items go
+    // out in rounds: round k hands the k-th item of every CTA that has one, in
+    // CTA order, from round_base[k] on. Items are in slot order, so early
+    // slots finish in the first rounds everywhere, and their h is published
+    // long before the down tasks (also in slot order) ask for it.
+    int pu, urem, pn, prem;
+    int round_base[kMaxRounds + 1];
     int tps;                   // down tiles per stage (1 or 2)
     int n_dn_stages;           // ceil(n_used / tps)
     size_t gu_stride, dn_stride;
@@ -207,7 +218,15 @@ __device__ inline void request_pairs(const unsigned long long* q, unsigned long 
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(pv[6]), "=l"(pv[7]) : "l"(q + 130) : "memory");
 }
 
-__device__ inline int gu_items_of(const FlowParams& p, int cta) { return p.gu_first[cta + 1] - p.gu_first[cta]; }
+__device__ inline int gu_items_of(const FlowParams& p, int cta) {
+    return cta < p.n_units ? p.pu + (cta < p.urem ? 1 : 0) : p.pn + (cta - p.n_units < p.prem ? 1 : 0);
+}
+// the gate/up item of CTA `cta` in round k
+__device__ inline int gu_item(const FlowParams& p, int cta, int k) {
+    if (cta < p.n_units) return p.round_base[k] + cta;
+    const int units_in_round = k < p.pu ? p.n_units : (k == p.pu ? p.urem : 0);
+    return p.round_base[k] + units_in_round + (cta - p.n_units);
+}
 
 // The tiles of this CTA's sequence number n: gate/up items (a stacked tile: 8
 // gate rows, then the same 8 up rows) and down stages (16 rows of the CTA's
@@ -224,7 +243,7 @@ __device__ inline Tiles stage_tiles(const FlowParams& p, int cta, int n, int per
     Tiles t{};
     d.bad = 0;
     if (idx < ng) {
-        const int item = p.gu_first[cta] + idx;
+        const int item = gu_item(p, cta, idx);
         const int rpb = p.ff / 8;
         d.a = item / rpb;
         d.b = item % rpb;
@@ -354,15 +373,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
         // h = silu(g) * u; every use: releases the stage to the producer. After
         // the down stages of a layer: the unit's combine, x_{L+1} = x_L + y.
         consumers_sync();
-        const int r = lane & 15;
+        // lane (hf, r): row r; half hf of the row's partials
+        const int r = lane & 15, hf = lane >> 4;
         const int row = cta * 16 + r;
+        const int spr = p.Gd / 2;   // super-blocks per down row
         float xr = 0.f;
         if (nd > 0) xr = p.accumulate ? p.out[row] : 0.f;
         bool ok = true;
         for (int L = 0; L < p.n_layers && ok; ++L) {
             const unsigned tag = (epoch << 6) + (unsigned)L + 1u;
             const FlowLayer& lb = p.layer[L];
-            // the layer's routing weights, lane e holding w[e], loaded before any wait
             const float wl = lane < p.n_used ? __ldg(lb.w + lane) : 0.f;
             for (int k = 0; k < per && ok; ++k) {
                 const int n = L * per + k, s = n % kStages;
@@ -370,9 +390,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 if (!ok) break;
                 const Desc d = descs[s];
                 if (k < ng) {
-                    float v = 0.f;
-                    if (lane < 16)
-                        for (int w = 0; w < p.G; ++w) v += red[(s * kNC + w) * 16 + lane];
+                    // row r's 16 warp partials (0 for warps past G), in a fixed order
+                    const float4* q = (const float4*)(red + (s * 16 + r) * kRedStride) + 2 * hf;
+                    const float4 q0 = q[0], q1 = q[1];
+                    float v = ((q0.x + q0.y) + (q0.z + q0.w)) + ((q1.x + q1.y) + (q1.z + q1.w));
+                    v += __shfl_xor_sync(0xffffffffu, v, 16);
                     const float u = __shfl_sync(0xffffffffu, v, (lane + 8) & 31);
                     __syncwarp();
                     if (lane == 0) {
@@ -393,8 +415,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 }
             }
             if (!ok || nd == 0) continue;
-            // every task of the unit is done: super-blocks in order, slots in order (weighted)
-            const int spr = p.Gd / 2;
+            // every task of the unit is done: y_r = sum over tasks of w(slot) *
+            // partial, in a fixed order; half hf takes tasks [16 hf, 16 hf + 16)
+            // of every 32
             float tot = 0.f;
             for (int e2 = 0; e2 < p.n_used; ++e2) {
                 float v = 0.f;
@@ -402,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 tot += __shfl_sync(0xffffffffu, wl, e2) * v;
             }
             xr = xr + tot;
-            __syncwarp();   // dred is read before the next layer's tasks may write it
+            __syncwarp();   // dred and wt are read before the next layer writes them
             if (lane < 16) {
                 if (L + 1 < p.n_layers)
                     st_pair(p.xpairs + (size_t)((L + 1) & 1) * p.d_model + row, xr, tag + 1u);
@@ -414,6 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
         // ------------------------------------------------------------ consumers
         uint32_t* table = (uint32_t*)(smem + Smem::table);
         fill_grid<kNC * 32>(table);
+        // the partials of warps past G are never written and sum as 0
+        for (int i = threadIdx.x; i < kStages * 16 * kRedStride; i += kNC * 32) red[i] = 0.f;
         consumers_sync();
         const uint32_t tab = grid_lane(table, lane);
         const int g = lane >> 2, c = lane & 3;
@@ -467,13 +492,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                     quad_sum(a0);
                     quad_sum(a1);
                     if (c == 0) {
-                        float* r0 = red + (s0 * kNC + warp) * 16;
-                        r0[g] = a0[0];
-                        r0[g + 8] = a0[1];
+                        float* r0 = red + (s0 * 16 + g) * kRedStride + warp;
+                        r0[0] = a0[0];
+                        r0[8 * kRedStride] = a0[1];
                         if (two) {
-                            float* r1 = red + (s1 * kNC + warp) * 16;
-                            r1[g] = a1[0];
-                            r1[g + 8] = a1[1];
+                            float* r1 = red + (s1 * 16 + g) * kRedStride + warp;
+                            r1[0] = a1[0];
+                            r1[8 * kRedStride] = a1[1];
                         }
                     }
                     __syncwarp();
@@ -494,10 +519,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 for (int t = warp; t < n_tasks; t += kNC) {
                     const int e = t / spr, sb = t % spr;
                     const int ds = e / p.tps, n = seq0 + ng + ds, s = n % kStages;
-                    float4 hv[2];
                     bool ready = true;
 #pragma unroll
                     for (int k = 0; k < 8; ++k) ready = ready && (unsigned)(pv[k] >> 32) == tag;
+                    float4 hv[2];
                     if (__all_sync(0xffffffffu, ready)) {
 #pragma unroll
                         for (int k = 0; k < 2; ++k)
@@ -620,27 +645,29 @@ int sb_try_flow_iq3s(const sb_decode_args& a, cudaStream_t st) {
     if (grid < p.n_units || grid > kMaxGrid) return 0;   // every down unit needs a CTA of its own
     // Gate/up items per CTA. A unit CTA also runs n_used * Gd down groups, a
     // gate/up item is G groups: the CTAs without a unit take about that many
-    // more items (in groups), and every unit CTA the same count, so the down
-    // units, and with them the next layer's x rows, finish together. Items go
-    // in slot order: the unit CTAs take the first slots, whose h the down
-    // tasks (also in slot order) need first.
+    // more items (in groups), so the down units, and with them the next
+    // layer's x rows, finish together.
     {
         const int n_items = a.n_used * a.ff / 8, units = p.n_units, rest = grid - units;
         const double extra = (double)(a.n_used * p.Gd) / p.G;   // a unit's down work, in items
-        int per_unit = (int)((n_items - rest * extra) / grid + 0.5);
-        per_unit = std::max(0, std::min(per_unit, n_items / units));
-        if (rest == 0) per_unit = n_items / grid;
-        int left = n_items - per_unit * units;
-        p.gu_first[0] = 0;
-        for (int c = 0; c < grid; ++c) {
-            int n;
-            if (rest > 0)
-                n = c < units ? per_unit : left / rest + ((c - units) < left % rest ? 1 : 0);
-            else
-                n = per_unit + (c < n_items - per_unit * grid ? 1 : 0);
-            p.gu_first[c + 1] = p.gu_first[c] + n;
+        double per_unit = std::floor((n_items - rest * extra) / grid + 0.5);
+        if (const char* v = std::getenv("SABAH_IQ3S_FLOW_GU_PER_UNIT"))   // tuning override
+            if (*v) per_unit = std::atof(v);
+        long unit_items = rest == 0 ? n_items : std::lround(per_unit * units);
+        unit_items = std::max(0l, std::min(unit_items, (long)n_items));
+        p.pu = (int)(unit_items / units);
+        p.urem = (int)(unit_items % units);
+        const int left = n_items - (int)unit_items;
+        p.pn = rest > 0 ? left / rest : 0;
+        p.prem = rest > 0 ? left % rest : 0;
+        const int rounds = std::max(p.pu + (p.urem > 0), p.pn + (p.prem > 0));
+        if (rounds > kMaxRounds) return 0;
+        p.round_base[0] = 0;
+        for (int k = 0; k < rounds; ++k) {
+            const int n = (k < p.pu ? units : k == p.pu ? p.urem : 0) + (k < p.pn ? rest : k == p.pn ? p.prem : 0);
+            p.round_base[k + 1] = p.round_base[k] + n;
         }
-        if (p.gu_first[grid] != n_items) return 0;
+        if (p.round_base[rounds] != n_items) return 0;
     }
 
     if (!g_fs.mem) {

@@ -178,6 +178,8 @@ bool sb_qt_supported(int qt) { return sb_block_elems(qt) != 0; }
 int sb_launch_mmid(const sb_mmid_args& a, cudaStream_t st) {
     const int taken = sb_try_mmid_iq3s(a, st);
     if (taken != 0) return taken > 0 ? 0 : -1;
+    const int q8 = sb_try_mmid_q8_0(a, st);
+    if (q8 != 0) return q8 > 0 ? 0 : -1;
     dim3 grid((a.rows + kRowsPerCta - 1) / kRowsPerCta, a.n_ids, a.n_tokens);
     auto l = [&](auto tag) { k_mmid_generic<decltype(tag)::value><<<grid, 256, 0, st>>>(a); };
     const int tslot = sb_timing_begin("mmid_generic", st);
@@ -209,6 +211,8 @@ int sb_launch_block(const sb_block_args& a, cudaStream_t st) {
     if (taken != 0) return taken > 0 ? 0 : -1;
     const int small = sb_try_block_small(a, st);
     if (small != 0) return small > 0 ? 0 : -1;
+    const int q8 = sb_try_block_q8_0(a, st);
+    if (q8 != 0) return q8 > 0 ? 0 : -1;
     dim3 g1((a.ff + kRowsPerCta - 1) / kRowsPerCta, a.n_used, a.n_tokens);
     bool ok;
     const int t1 = sb_timing_begin("gate_up_generic", st);

@@ -307,6 +307,103 @@ __device__ inline void do_pair(uint32_t tile, int q, uint32_t setB, const Lane& 
     }
 }
 
+// ---------------------------------------------------------------- Q8_0 decode
+// The same engine for Q8_0 (34-byte blocks of 32 weights: fp16 d, then 32
+// int8): a block is a sub-block of the K permutation (quad c owns block
+// 4q + c of group q), so the x sets and MMA chains are those of IQ3_S. In
+// shared memory a tile's rows come in pairs (2g, 2g + 1), one bulk copy each,
+// at a padded pair stride, so a warp's loads of rows 2g (g = 0..7) spread over
+// the banks; lane (g, c) decodes rows 2g (h = 0) and 2g + 1 (h = 1).
+struct LaneQ8 {
+    uint32_t row;     // tile-relative offset of row 2g (row 2g + 1 is rb further)
+    uint32_t rb;
+    uint32_t qoff;    // 34c + 2 rounded down to 4: block c's first aligned quant word
+    uint32_t dof;     // 34c: block c's scale
+    uint32_t sel;     // PRMT selector for 4 quants from words (j, j + 1)
+    uint32_t invd;    // as Lane::invd
+};
+__device__ inline LaneQ8 lane_init_q8(int rb, int pair_stride, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    const int boff = (g >> 1) == c ? (2 * c + (g & 1)) * 8 : 64;
+    LaneQ8 L;
+    L.row = (uint32_t)(g * pair_stride);
+    L.rb = (uint32_t)rb;
+    L.dof = (uint32_t)(34 * c);
+    L.qoff = (uint32_t)((34 * c + 2) & ~3);
+    L.sel = (c & 1) ? 0x3210u : 0x5432u;   // c odd: block c's quants are word-aligned
+    L.invd = (uint32_t)(4 * c - boff);
+    return L;
+}
+
+__device__ inline uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+// Weights 4S .. 4S + 3 of a block (words w0, w1 around them) as two fp16
+// pairs: biased bytes b = q + 128 placed under exponent 0x64 give 1024 + b
+// exactly; subtracting 1152 leaves q.
+__device__ inline void q8_entry(uint32_t w0, uint32_t w1, uint32_t sel, uint32_t& a0, uint32_t& a1) {
+    const uint32_t u = prmt(w0, w1, sel) ^ 0x80808080u;
+    a0 = hsub2_u32(prmt(u, 0x64646464u, 0x4140u), 0x64806480u);
+    a1 = hsub2_u32(prmt(u, 0x64646464u, 0x4342u), 0x64806480u);
+}
+
+// Step S (weights 4S .. 4S + 3 of every block) of both groups of a Q8_0 pair;
+// w holds word S of each (group, row) and advances to word S + 1.
+template <int S>
+__device__ inline void step_q8(uint32_t setq, uint32_t sel, const uint32_t (&base)[2][2], uint32_t (&w)[2][2],
+                               float (&dd)[2][4]) {
+    const uint2 bv[2] = {ld_v2<S * kRecBytes>(setq), ld_v2<kGroupBytes + S * kRecBytes>(setq)};
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        uint32_t a[2][2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t wn = ld_u32<4 * (S + 1)>(base[n][h]);
+            q8_entry(w[n][h], wn, sel, a[h][0], a[h][1]);
+            w[n][h] = wn;
+        }
+        mma16816(dd[n], a[0][0], a[1][0], a[0][1], a[1][1], bv[n].x, bv[n].y);
+    }
+}
+template <int... S>
+__device__ inline void all_steps_q8(std::integer_sequence<int, S...>, uint32_t setq, uint32_t sel,
+                                    const uint32_t (&base)[2][2], uint32_t (&w)[2][2], float (&dd)[2][4]) {
+    (step_q8<S>(setq, sel, base, w, dd), ...);
+}
+
+// Group pair (q, q + 1) of a Q8_0 tile: blocks 4q + c and 4q + 4 + c of rows
+// 2g and 2g + 1; adds their dots into acc[0] (row 2g) and acc[1] (row 2g + 1).
+__device__ inline void do_pair_q8(uint32_t tile, int q, uint32_t setB, const LaneQ8& L, float (&acc)[2]) {
+    const uint32_t setq = setB + (uint32_t)q * kGroupBytes;
+    const uint32_t invq = setq + L.invd;
+    uint32_t base[2][2], w[2][2];
+    float db[2][2];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        // the set's inverse scale carries 2^24 for IQ3_S's subnormal weights; Q8_0 quants are plain fp16
+        const float inv = ld_f32<8 * kRecBytes>(invq + (uint32_t)n * kGroupBytes) * (1.0f / 16777216.0f);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t blk = tile + L.row + (uint32_t)h * L.rb + (uint32_t)(q + n) * 136u;
+            base[n][h] = blk + L.qoff;
+            w[n][h] = ld_u32<0>(base[n][h]);
+            db[n][h] = __half2float(__ushort_as_half((unsigned short)ld_u16<0>(blk + L.dof))) * inv;
+        }
+    }
+    float dd[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) dd[n][0] = dd[n][1] = dd[n][2] = dd[n][3] = 0.f;
+    all_steps_q8(std::make_integer_sequence<int, 8>{}, setq, L.sel, base, w, dd);
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        acc[0] = fmaf(db[n][0], dd[n][0] + dd[n][1], acc[0]);
+        acc[1] = fmaf(db[n][1], dd[n][2] + dd[n][3], acc[1]);
+    }
+}
+
 // Replicated grid table: entry e, replica r at word e * kReplicas + r. Threads
 // 0..NT-1 fill it.
 template <int NT, int R = kReplicas>

@@ -78,6 +78,10 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force 
 // many (token, slot) pairs on device-resident banks; same return convention
 int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st);
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st);
+// Q8_0 on the same tensor-core matvec engine (sb_mmid_iq3s.cu): MUL_MAT_ID,
+// and the fused block as two launches; same return convention
+int sb_try_mmid_q8_0(const sb_mmid_args& a, cudaStream_t st);
+int sb_try_block_q8_0(const sb_block_args& a, cudaStream_t st);
 // Q4_K / Q6_K fused block for 1-4 tokens on device banks, each distinct routed
 // expert decoded once per block (sb_small_kq.cu): 1 taken, 0 not covered, -1 error
 int sb_try_block_small(const sb_block_args& a, cudaStream_t st);

@@ -78,10 +78,22 @@ struct Desc {
     int which;     // gate/up: 0 gate, 1 up
 };
 
+// Per weight format: IQ3_S needs the grid table; Q8_0 needs none and gives
+// its room (and the rest of the budget) to the tile ring, since its tiles are
+// 2.5x larger (34,816 B for k = 2048).
+constexpr int kSmemBudget = 227 * 1024;
+constexpr int kFixedBytes = kSets * kSetBytes + kRedSlots * kMaxWpt * 16 * 4 + kMaxStages * (int)sizeof(Desc) +
+                            kRedSlots * 4 + 8 + 2 * kMaxStages * 8;
+template <int QT>
+struct Fmt {
+    static constexpr int table_bytes = QT == SB_IQ3_S ? kTableBytes : 0;
+    static constexpr int ring_bytes = QT == SB_IQ3_S ? kRingBytes : ((kSmemBudget - kFixedBytes - 8) & ~127);
+};
+template <int QT>
 struct Smem {
     static constexpr int table = 0;
-    static constexpr int stages = table + kTableBytes;
-    static constexpr int sets = stages + kRingBytes;
+    static constexpr int stages = table + Fmt<QT>::table_bytes;
+    static constexpr int sets = stages + Fmt<QT>::ring_bytes;
     static constexpr int red = sets + kSets * kSetBytes;                  // [kRedSlots][kMaxWpt][16] floats
     static constexpr int desc = red + kRedSlots * kMaxWpt * 16 * 4;      // [kMaxStages] Desc
     static constexpr int cnt = desc + kMaxStages * (int)sizeof(Desc);    // [kRedSlots] ints
@@ -89,7 +101,8 @@ struct Smem {
     static constexpr int bars = (abort_flag + 4 + 7) & ~7;                // full[kMaxStages], empty[kMaxStages]
     static constexpr int total = bars + 2 * kMaxStages * 8;
 };
-static_assert(Smem::total <= 227 * 1024, "shared memory budget");
+static_assert(Smem<SB_IQ3_S>::total <= kSmemBudget && Smem<SB_Q8_0>::total <= kSmemBudget, "shared memory budget");
+static_assert(Smem<SB_Q8_0>::stages % 128 == 0 && Smem<SB_Q8_0>::sets % 16 == 0, "Q8_0 ring alignment");
 
 struct Params {
     int mode;
@@ -97,8 +110,13 @@ struct Params {
     int per_key;           // consecutive items sharing one x vector
     int wpt, gpw, P;       // warps per item, groups per warp, items in flight (12 / wpt)
     int k, rb, rtiles;     // row length, row bytes, 16-row tiles per matrix
-    int n_stages;          // ring stages (multiple of kIssuers, <= kMaxStages)
-    int stage_bytes;       // 16 * rb rounded up to 128
+    int n_stages;          // ring stages (multiple of issuers, <= kMaxStages)
+    int issuers;           // producer lanes; lane l owns stages l, l + issuers, ...
+    int stage_bytes;       // one tile in shared memory, rounded up to 128
+    // a tile arrives as `copies` bulk copies of copy_bytes, from global rows
+    // copy_src bytes apart to stage offsets copy_dst apart (IQ3_S: one copy of
+    // 16 rows; Q8_0: 8 copies of a row pair at a bank-spreading pair stride)
+    int copies, copy_bytes, copy_src, copy_dst;
     sb_mmid_args m;
     sb_block_args b;
     float* partial;        // DOWN: [T][n_used][d_model]; GATE_UP: [T][n_used][2][ff]
@@ -151,7 +169,9 @@ __device__ inline const float* key_vector(const Params& p, int key) {
 }
 
 // ---------------------------------------------------------------- the kernel
+template <int QT>
 __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
+    using Smem = ::Smem<QT>;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* bars = (uint64_t*)(smem + Smem::bars);
@@ -189,11 +209,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
         // lane l issues sequence numbers n = l, l + kIssuers, ... (stage n % ns,
         // always the same lane for a given stage); each lane looks up its own
         // tiles' expert addresses, so those loads overlap across lanes
-        if (lane < kIssuers) {
+        if (lane < p.issuers) {
             const uint32_t st0 = smem_u32(smem + Smem::stages);
             const uint32_t bytes = 16u * p.rb;
             int last = -1;
-            for (int n = lane; i0 + n < i1 && !*abort_flag; n += kIssuers) {
+            for (int n = lane; i0 + n < i1 && !*abort_flag; n += p.issuers) {
                 const int s = n % ns;
                 if (n >= ns && !mbar_wait(empty0 + 8 * s, ((n / ns) - 1) & 1, p.err, abort_flag)) break;
                 const int item = i0 + n;
@@ -207,7 +227,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
                 *(volatile int*)&descs[s].seq = n;   // the stage's previous tile is released
                 if (!d.bad) {
                     mbar_expect_tx(full0 + 8 * s, bytes);
-                    bulk_g2s(st0 + s * p.stage_bytes, src, bytes, full0 + 8 * s);
+                    for (int j = 0; j < p.copies; ++j)
+                        bulk_g2s(st0 + s * p.stage_bytes + j * p.copy_dst, src + (size_t)j * p.copy_src, p.copy_bytes,
+                                 full0 + 8 * s);
                 } else {
                     mbar_arrive(full0 + 8 * s);
                 }
@@ -215,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
             }
             // never leave with copies in flight: the last use of each of this
             // lane's stages must have landed
-            for (int n = std::max(lane, last - ns + kIssuers); n <= last; n += kIssuers)
+            for (int n = std::max(lane, last - ns + p.issuers); n <= last; n += p.issuers)
                 for (long long i = 0; i < kSpinLimit && !mbar_try_wait(full0 + 8 * (n % ns), (n / ns) & 1); ++i) {
                 }
         }
@@ -224,13 +246,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
 
     // ---------------------------------------------------------- consumers
     uint32_t* table = (uint32_t*)(smem + Smem::table);
-    fill_table<kConsumers * 32>(table);
+    if constexpr (QT == SB_IQ3_S) fill_table<kConsumers * 32>(table);
     // activations and outputs only after the previous kernel on the stream is done
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int g = lane >> 2, c = lane & 3;
     const uint32_t boff = lane_boff(lane);
-    const Lane L = lane_init(table, p.rb, lane);
+    Lane L{};
+    LaneQ8 LQ{};
+    if constexpr (QT == SB_IQ3_S)
+        L = lane_init(table, p.rb, lane);
+    else
+        LQ = lane_init_q8(p.rb, p.copy_dst, lane);
     const uint32_t stages32 = smem_u32(smem + Smem::stages), sets32 = smem_u32(smem + Smem::sets);
     const int pos = warp / p.wpt;   // which of the P items in flight
     const int wsub = warp % p.wpt;  // which part of the row
@@ -266,8 +293,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
             const int bad = !stamped ? -1 : !landed ? SB_DERR_TIMEOUT : d.bad;
             float acc[2] = {0.f, 0.f};
             if (!bad)
-                for (int q = wsub * p.gpw; q < (wsub + 1) * p.gpw; q += 2)
-                    do_pair(stages32 + s * p.stage_bytes, q, sets32 + d.slot * kSetBytes + boff, L, acc);
+                for (int q = wsub * p.gpw; q < (wsub + 1) * p.gpw; q += 2) {
+                    if constexpr (QT == SB_IQ3_S)
+                        do_pair(stages32 + s * p.stage_bytes, q, sets32 + d.slot * kSetBytes + boff, L, acc);
+                    else
+                        do_pair_q8(stages32 + s * p.stage_bytes, q, sets32 + d.slot * kSetBytes + boff, LQ, acc);
+                }
             // this warp's rows: reduce the 4 quads, publish, count
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -276,8 +307,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
             }
             float* rr = red + (s * kMaxWpt + wsub) * 16;
             if (c == 0) {
-                rr[g] = acc[0];
-                rr[g + 8] = acc[1];
+                // tile rows of (g, h): IQ3_S g and g + 8, Q8_0 2g and 2g + 1
+                const int r0 = QT == SB_IQ3_S ? g : 2 * g, r1 = QT == SB_IQ3_S ? g + 8 : 2 * g + 1;
+                rr[r0] = acc[0];
+                rr[r1] = acc[1];
             }
             __threadfence_block();
             __syncwarp();
@@ -379,29 +412,64 @@ bool plan_groups(int k, int& wpt, int& gpw) {
     return false;
 }
 
+// Tile geometry of a format: stage size and the bulk copies that fill a stage.
+template <int QT>
+void tile_geometry(Params& p) {
+    if (QT == SB_IQ3_S) {
+        p.copies = 1;
+        p.copy_bytes = 16 * p.rb;
+        p.copy_src = 0;
+        p.copy_dst = 0;
+        p.stage_bytes = (16 * p.rb + 127) & ~127;
+    } else {
+        // row pairs at a stride of 12 (mod 32) words, at least 4 bytes of pad:
+        // a lane's last word load may run past its pair
+        const int words = 2 * p.rb / 4;
+        int pad = ((12 - words % 32) + 32) % 32 * 4;
+        if (pad < 4) pad += 128;
+        p.copies = 8;
+        p.copy_bytes = 2 * p.rb;
+        p.copy_src = 2 * p.rb;
+        p.copy_dst = 2 * p.rb + pad;
+        p.stage_bytes = (8 * p.copy_dst + 127) & ~127;
+    }
+}
+
+template <int QT>
 int launch(Params& p, cudaStream_t st) {
+    using Smem = ::Smem<QT>;
     int dev = 0;
     if (!sb_cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return -1;
     if (dev < 0 || dev >= kMaxDevices) {
-        sb_set_error("the IQ3_S kernels support devices 0..%d", kMaxDevices - 1);
+        sb_set_error("the tensor-core matvec kernels support devices 0..%d", kMaxDevices - 1);
         return -1;
     }
-    if (!g_attr_set[dev]) {
-        if (!sb_cuda_ok(cudaFuncSetAttribute(k_iq3s, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total),
-                        "iq3s smem attribute"))
+    static bool attr_set[kMaxDevices] = {};
+    if (!attr_set[dev]) {
+        if (!sb_cuda_ok(cudaFuncSetAttribute(k_iq3s<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total),
+                        "matvec smem attribute"))
             return -1;
-        if (!sb_cuda_ok(cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev),
-                        "SM count"))
-            return -1;
-        g_attr_set[dev] = true;
+        if (!g_attr_set[dev]) {
+            if (!sb_cuda_ok(cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev),
+                            "SM count"))
+                return -1;
+            g_attr_set[dev] = true;
+        }
+        attr_set[dev] = true;
     }
     p.P = kConsumers / p.wpt;
-    p.stage_bytes = (16 * p.rb + 127) & ~127;
-    p.n_stages = std::min(kMaxStages, (kRingBytes / p.stage_bytes) / kIssuers * kIssuers);
+    tile_geometry<QT>(p);
+    const int fit = Fmt<QT>::ring_bytes / p.stage_bytes;
+    p.issuers = std::min(kIssuers, fit);
+    if (p.issuers < 1) {
+        sb_set_error("tile of %d bytes does not fit the ring", p.stage_bytes);
+        return -1;
+    }
+    p.n_stages = std::min(kMaxStages, fit / p.issuers * p.issuers);
     const int grid = std::max(1, std::min(p.n_items, g_num_sms[dev]));
-    const int tslot = sb_timing_begin(p.mode == MODE_MMID ? "mmid_iq3s" : p.mode == MODE_GATE_UP ? "gate_up_iq3s"
-                                                                                                  : "down_iq3s",
-                                      st);
+    const char* names[3][2] = {{"mmid_iq3s", "mmid_q8_0"}, {"gate_up_iq3s", "gate_up_q8_0"},
+                               {"down_iq3s", "down_q8_0"}};
+    const int tslot = sb_timing_begin(names[p.mode][QT == SB_IQ3_S ? 0 : 1], st);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -412,9 +480,13 @@ int launch(Params& p, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_iq3s, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_iq3s<QT>, p);
     sb_timing_end(tslot, st);
-    return sb_cuda_ok(e, "iq3s launch") ? 1 : -1;
+    return sb_cuda_ok(e, "matvec launch") ? 1 : -1;
+}
+
+int launch(Params& p, int qt, cudaStream_t st) {
+    return qt == SB_IQ3_S ? launch<SB_IQ3_S>(p, st) : launch<SB_Q8_0>(p, st);
 }
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -493,14 +565,19 @@ static __device__ __align__(256) uint8_t sb_fixed_scratch[kFixedScratchBytes];
 
 void sb_block_scratch_invalidate() { g_bs.stale = g_bs.mem != nullptr; }
 
-int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
-    if (a.qt != SB_IQ3_S || !fast_path_enabled()) return 0;
-    const int grouped = sb_try_mmid_iq3s_grouped(a, st);   // prefill-sized calls
-    if (grouped != 0) return grouped;
+namespace {
+// Tiles of this size fit the format's ring (IQ3_S: the historical 16 x 880 B cap)
+bool tile_fits(int qt, size_t rb) {
+    return qt == SB_IQ3_S ? 16 * rb <= (size_t)kMaxTileBytes : 16 * rb <= (size_t)Fmt<SB_Q8_0>::ring_bytes / 4;
+}
+
+int block_two_launches(const sb_block_args& a, int qt, cudaStream_t st);
+
+int try_mmid(const sb_mmid_args& a, cudaStream_t st) {
     int wpt, gpw;
     if (!plan_groups(a.k, wpt, gpw) || a.rows % 16) return 0;
-    const size_t rb = sb_row_bytes_of(SB_IQ3_S, a.k);
-    if (a.row_stride != rb || 16 * rb > (size_t)kMaxTileBytes) return 0;
+    const size_t rb = sb_row_bytes_of(a.qt, a.k);
+    if (a.row_stride != rb || !tile_fits(a.qt, rb)) return 0;
     if (!a.ex.ptrs && (!aligned16(a.ex.base) || a.ex.expert_stride % 16)) return 0;
     if (a.x_id_stride % 16 || a.x_token_stride % 16 || !aligned16(a.x)) return 0;
     const long long items = (long long)a.n_ids * a.n_tokens * (a.rows / 16);
@@ -516,7 +593,20 @@ int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
     p.rb = (int)rb;
     p.m = a;
     p.err = a.err;
-    return launch(p, st);
+    return launch(p, a.qt, st);
+}
+}  // namespace
+
+int sb_try_mmid_iq3s(const sb_mmid_args& a, cudaStream_t st) {
+    if (a.qt != SB_IQ3_S || !fast_path_enabled()) return 0;
+    const int grouped = sb_try_mmid_iq3s_grouped(a, st);   // prefill-sized calls
+    if (grouped != 0) return grouped;
+    return try_mmid(a, st);
+}
+
+int sb_try_mmid_q8_0(const sb_mmid_args& a, cudaStream_t st) {
+    if (a.qt != SB_Q8_0 || !fast_path_enabled()) return 0;
+    return try_mmid(a, st);
 }
 
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
@@ -560,12 +650,24 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
         const int taken = sb_try_decode_iq3s(d, st);
         if (taken != 0) return taken;
     }
+    return block_two_launches(a, SB_IQ3_S, st);
+}
+
+int sb_try_block_q8_0(const sb_block_args& a, cudaStream_t st) {
+    if (a.qt_gate != SB_Q8_0 || a.qt_up != SB_Q8_0 || a.qt_down != SB_Q8_0 || !fast_path_enabled()) return 0;
+    return block_two_launches(a, SB_Q8_0, st);
+}
+
+namespace {
+// gate/up + SwiGLU, then down + weighted combine: one launch each, over the
+// shared block scratch
+int block_two_launches(const sb_block_args& a, int qt, cudaStream_t st) {
     if (a.xrows) return 0;   // the launches below read rows t only
     int wpt_g, gpw_g, wpt_d, gpw_d;
     if (!plan_groups(a.d_model, wpt_g, gpw_g) || !plan_groups(a.ff, wpt_d, gpw_d)) return 0;
     if (a.ff % 16 || a.d_model % 16) return 0;
-    const size_t rbg = sb_row_bytes_of(SB_IQ3_S, a.d_model), rbd = sb_row_bytes_of(SB_IQ3_S, a.ff);
-    if (16 * rbg > (size_t)kMaxTileBytes || 16 * rbd > (size_t)kMaxTileBytes) return 0;
+    const size_t rbg = sb_row_bytes_of(qt, a.d_model), rbd = sb_row_bytes_of(qt, a.ff);
+    if (!tile_fits(qt, rbg) || !tile_fits(qt, rbd)) return 0;
     for (const sb_experts* e : {&a.gate, &a.up, &a.down})
         if (!e->ptrs && (!aligned16(e->base) || e->expert_stride % 16)) return 0;
     if (!aligned16(a.x) || !aligned16(a.h) || (a.d_model * 4) % 16 || (a.ff * 4) % 16) return 0;
@@ -585,7 +687,7 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     p.rb = (int)rbg;
     p.partial = g_bs.gu_partial;
     p.counters = g_bs.gu_counters;
-    if (launch(p, st) < 0) return -1;
+    if (launch(p, qt, st) < 0) return -1;
     // down + weighted combine: items (t, e, row tile)
     p.mode = MODE_DOWN;
     p.rtiles = a.d_model / 16;
@@ -597,8 +699,9 @@ int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     p.rb = (int)rbd;
     p.partial = g_bs.dn_partial;
     p.counters = g_bs.dn_counters;
-    return launch(p, st);
+    return launch(p, qt, st);
 }
+}  // namespace
 
 int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S) {
@@ -662,7 +765,7 @@ int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st) {
     p.rb = (int)sb_row_bytes_of(SB_IQ3_S, a.d_model);
     p.partial = (float*)(fs.ptr + kFixedCounterBytes);
     p.counters = (int*)fs.ptr;
-    if (launch(p, st) < 0) return -1;
+    if (launch<SB_IQ3_S>(p, st) < 0) return -1;
     p.mode = MODE_DOWN;
     p.rtiles = a.d_model / 16;
     p.n_items = a.n_tokens * a.n_used * p.rtiles;
@@ -673,5 +776,5 @@ int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st) {
     p.rb = (int)sb_row_bytes_of(SB_IQ3_S, a.ff);
     p.partial = (float*)(fs.ptr + kFixedCounterBytes + gup);
     p.counters = (int*)(fs.ptr + guc);
-    return launch(p, st) < 0 ? -1 : 0;
+    return launch<SB_IQ3_S>(p, st) < 0 ? -1 : 0;
 }

@@ -10,7 +10,7 @@ N(0,1) per layer (seed 100 + L) -> softmax -> top-10 -> renormalised; x ~ N(0,1)
 seeded one) are cycled so every step reads 973 MB of distinct expert bytes,
 more than the 126 MB L2: no L2 reuse between timed steps.
 
-A step = one token through all 48 blocks (96 kernel launches). `value` is
+A step = one token through all 48 blocks (one persistent kernel launch). `value` is
 device-timed (CUDA events on the launching stream, CUDA-graph replay, inputs
 resident); `e2e` goes through the public C ABI per step (sabah_moe_decode) with
 the step's inputs copied from pinned host memory and the result copied back.
@@ -46,7 +46,7 @@ WORKLOAD = "cfg2: IQ3_S decode, 1 token x 48 blocks, 512 experts/block, top-10, 
 # DRAM bytes (read + write) per decoded block of the persistent decode kernels,
 # from one ncu capture each on the 2-block case (profiles/), keyed by the
 # runtime's kernel-timing name
-DRAM_BYTES_PER_BLOCK = {"decode_iq3s": (40.62e6 + 0.27e6) / 2}
+DRAM_BYTES_PER_BLOCK = {"decode_iq3s": (40.62e6 + 0.27e6) / 2, "decode_iq3s_flow": (40.88e6 + 0.24e6) / 2}
 
 
 def iq3s_row_bytes(k: int) -> int:
@@ -780,7 +780,41 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
 ST_LAYERS, ST_SLAB = 16, 9.8e9
 ST_METRIC = "MoE MUL_MAT_ID tokens/s (IQ3_S decode, host-resident bank streamed into a 9.8 GB hot-tier slab)"
 ST_WORKLOAD = ("cfg5s: IQ3_S decode, 1 token x 16 blocks through sabah_rt_mul_mat_id_v2 (gate, up, down; host "
-               "sources), 16.6 GB pinned host bank, 9.8 GB hot-tier slab, Zipf(1.1) expert popularity per block")
+               "sources), 16.6 GB bank in a file mapped read-only (misses read from disk through the pinned "
+               "staging ring, O_DIRECT where the file system allows), 9.8 GB hot-tier slab, Zipf(1.1) expert "
+               "popularity per block")
+ST_WORKLOAD_PINNED = ("cfg5s (--source pinned): as cfg5s, the 16.6 GB bank in pinned host memory instead of a "
+                      "file (misses by direct DMA)")
+
+
+def disk_read_gbs(path: str, nbytes: int = 1 << 30) -> float | None:
+    """O_DIRECT sequential read rate of the bank file (1 GiB from its middle),
+    the roofline of misses served from disk; None if the file system refuses
+    O_DIRECT."""
+    import mmap
+    try:
+        fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+    except OSError:
+        return None
+    try:
+        size = os.fstat(fd).st_size
+        chunk = 8 << 20
+        buf = mmap.mmap(-1, chunk)   # page-aligned
+        off = (size // 2) & ~(chunk - 1)
+        nbytes = min(nbytes, (size - off) & ~(chunk - 1))
+        t0 = time.perf_counter()
+        done = 0
+        while done < nbytes:
+            n = os.preadv(fd, [buf], off + done)
+            if n <= 0:
+                break
+            done += n
+        dt = time.perf_counter() - t0
+        return done / dt / 1e9 if dt > 0 else None
+    except OSError:
+        return None
+    finally:
+        os.close(fd)
 
 
 def stream_routing(n_tok: int, layers: int, seed: int = 51):
@@ -816,9 +850,27 @@ def run_stream(args, rank: int, world: int, local_rank: int):
     L = rt.lib()
     stream = torch.cuda.Stream(device=dev)
     layer_bytes = EXPERTS * (2 * GU_EXPERT + D_EXPERT)
-    host = torch.empty(ST_LAYERS * layer_bytes, dtype=torch.uint8, pin_memory=True)
+    from_file = args.source == "file"
+    bank_path = None
+    source_note = None
+    if from_file:
+        # the bank goes to a file next to the repository (the box's local disk),
+        # written through one pinned bounce buffer, then mapped read-only
+        import shutil
+        bank_dir = os.environ.get("SABAH_BENCH_BANK_DIR", os.path.join(ROOT, "_bank"))
+        os.makedirs(bank_dir, exist_ok=True)
+        free = shutil.disk_usage(bank_dir).free
+        if free < 1.1 * ST_LAYERS * layer_bytes:
+            from_file = False
+            source_note = "pinned: %.1f GB free at %s, below the bank's size" % (free / 1e9, bank_dir)
+    if from_file:
+        bank_path = os.path.join(bank_dir, "cfg5s_bank.bin")
+        bounce = torch.empty(EXPERTS * GU_EXPERT, dtype=torch.uint8, pin_memory=True)
+        fh = open(bank_path, "wb")
+    else:
+        host = torch.empty(ST_LAYERS * layer_bytes, dtype=torch.uint8, pin_memory=True)
     tmp = torch.empty(EXPERTS * GU_EXPERT, dtype=torch.uint8, device=dev)
-    views = []
+    spans = []
     with torch.cuda.stream(stream):
         for Lr in range(ST_LAYERS):
             parts = []
@@ -827,11 +879,29 @@ def run_stream(args, rank: int, world: int, local_rank: int):
                 ops.synth_rows(EXPERTS * rows, k, QT_IQ3_S, seed=(60 + Lr) * 4 + role, sigma=0.02, out=tmp[:n],
                                stream=stream)
                 off = Lr * layer_bytes + role * EXPERTS * GU_EXPERT
-                host[off:off + n].copy_(tmp[:n], non_blocking=True)
-                parts.append(host[off:off + n])
-            views.append(parts)
+                if from_file:
+                    bounce[:n].copy_(tmp[:n], non_blocking=True)
+                    stream.synchronize()
+                    fh.seek(off)
+                    fh.write(memoryview(bounce[:n].numpy()))
+                else:
+                    host[off:off + n].copy_(tmp[:n], non_blocking=True)
+                parts.append((off, n))
+            spans.append(parts)
     stream.synchronize()
     del tmp
+    if from_file:
+        fh.flush()
+        os.fsync(fh.fileno())
+        fh.close()
+        del bounce
+        bank = np.memmap(bank_path, dtype=np.uint8, mode="r")
+        disk_gbs = disk_read_gbs(bank_path)
+        host = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)   # the copy-peak probe below
+        views = [[bank[o:o + n] for o, n in parts] for parts in spans]
+    else:
+        disk_gbs = None
+        views = [[host[o:o + n] for o, n in parts] for parts in spans]
     # measured pinned H2D copy bandwidth: the roofline of the misses
     probe_h = host[: 1 << 30]
     probe_d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
@@ -898,19 +968,31 @@ def run_stream(args, rank: int, world: int, local_rank: int):
     misses = (s1["misses"] - s0["misses"]) / args.steps
     hits = (s1["hits"] - s0["hits"]) / args.steps
     fill_gbs = fetched / (ms * 1e-3) / 1e9
+    fill_io = {k: s1[k] - s0[k] for k in ("staged_bytes", "pinned_fill_bytes", "direct_io_reads", "direct_io_bytes",
+                                          "direct_io_fallbacks", "fill_waves")}
     del host, views
+    if from_file:
+        del bank
+        try:
+            os.remove(bank_path)
+        except OSError:
+            pass
     return {
         "metric": ST_METRIC, "value": round(1e3 / ms, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": warm, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (N(0,0.02) weights IQ3_S-encoded, copied to pinned host memory; Zipf(1.1) routing)",
-        "config": {"workload": ST_WORKLOAD, "layers": ST_LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
+        "data": "synthetic (N(0,0.02) weights IQ3_S-encoded, written to %s; Zipf(1.1) routing)"
+                % ("a bank file" if from_file else "pinned host memory"),
+        "config": {"workload": ST_WORKLOAD if from_file else ST_WORKLOAD_PINNED, "layers": ST_LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
                    "top_k": TOP_K, "slab_bytes": int(float(os.environ["SABAH_LLAMA_HOT_BYTES"])),
                    "host_bank_bytes": ST_LAYERS * layer_bytes, "tokens_per_step": 1,
                    "l2": "bank 16.6 GB in host memory, slab 9.8 GB, both far above L2"},
         "roofline": {"bound": "pcie", "achieved": round(fill_gbs, 2), "peak": round(h2d_gbs, 1), "unit": "GB/s",
                      "frac": round(fill_gbs / h2d_gbs, 4), "traffic": int(fetched),
                      "peak_kind": "measured in this run: pinned host-to-device copy of 1 GiB",
+                     "disk_read_gbs": None if disk_gbs is None else round(disk_gbs, 2),
+                     "source": "file" if from_file else (source_note or "pinned"),
+                     "fill_io_per_run": fill_io,
                      "misses_per_token": round(misses, 1), "hits_per_token": round(hits, 1)},
         "e2e": {"value": round(1e3 / ms, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(x0_h.numel() * 4 + fetched),
                 "d2h_bytes_per_step": int(out_h.numel() * 4 + ST_LAYERS * TOP_K * 4),
@@ -1305,6 +1387,8 @@ def main():
                          "cfg2: the headline 1-token decode (replicas for N > 1); cfg3: 512-token prefill "
                          "of one block; cfg4: Q4_K/Q6_K batch-4 decode; cfg5: expert-parallel bank; cfg5s: "
                          "host-resident bank streamed through the hot-tier slab")
+    ap.add_argument("--source", default="file", choices=["file", "pinned"],
+                    help="cfg5s: where the host bank lives (a mapped file, or pinned host memory)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="blocks per token; fewer than 48 only for small profiling cases (not the benchmark)")
     args = ap.parse_args()

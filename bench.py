@@ -529,9 +529,21 @@ def run_ep(args, rank: int, world: int, local_rank: int):
             banks.append(tuple(parts))
     stream.synchronize()
     ids_np, w_np = routing_tokens(EP_SETS, EP_TOKENS, LAYERS)
-    host_plans = [[ep.plan_layer(ids_np[s, Lr], w_np[s, Lr], rank, world, EXPERTS) for Lr in range(LAYERS)]
-                  for s in range(EP_SETS)]
-    plans = [[ep.plan_to_device(pl) for pl in hp] for hp in host_plans]
+    exchange = args.exchange
+
+    def plan_step(s):
+        """the host plans of routing set s (all layers) and their packed device copy"""
+        if exchange == "ag":
+            hp = [ep.plan_layer(ids_np[s, Lr], w_np[s, Lr], rank, world, EXPERTS) for Lr in range(LAYERS)]
+            return hp, ep.pack_plans(hp)
+        hp = [ep.plan_layer_a2a(ids_np[s, Lr], w_np[s, Lr], rank, world, EXPERTS) for Lr in range(LAYERS)]
+        return hp, ep.pack_plans_a2a(hp)
+
+    host_plans, plans = [], []
+    for s in range(EP_SETS):
+        hp, dp = plan_step(s)
+        host_plans.append(hp)
+        plans.append(dp)
     t0, t1 = ep.token_range(rank, EP_TOKENS, world)
     x_all0 = np.random.default_rng(40).standard_normal((EP_TOKENS, D_MODEL)).astype(np.float32)
     x0_own = torch.from_numpy(x_all0[t0:t1]).to(dev)
@@ -541,7 +553,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
 
     def step(s):
         x.copy_(x0_own)
-        ep.decode_step(x, plans[s], kops, comm)
+        ep.decode_step(x, plans[s], kops, comm, exchange)
 
     def barrier():
         if world > 1:
@@ -600,7 +612,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
     launches_per_step = sum(v[0] for v in ktimes.values())
     # algorithmic bytes: each distinct local expert of a block read once per step
     # (the pair kernels read an expert once per routed pair; see traffic)
-    distinct = [[int(np.unique(pl.lid).size) for pl in hp] for hp in host_plans]
+    distinct = [[int(np.unique(pl.lid).size) for pl in hp] for hp in host_plans]   # same experts either way
     alg_bytes = [sum(n * (2 * GU_EXPERT + D_EXPERT) for n in ds) for ds in distinct]
     pair_bytes = [sum(pl.n_pairs * (2 * GU_EXPERT + D_EXPERT) for pl in hp) for hp in host_plans]
     bytes_step = float(np.mean(alg_bytes))
@@ -616,19 +628,17 @@ def run_ep(args, rank: int, world: int, local_rank: int):
                 "bytes_per_step_all_gpus": int(totals[0].item()), "pair_bytes_per_step_all_gpus": int(totals[1].item()),
                 "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)} for k, v in ktimes.items()}}
 
-    # e2e: host ids planned per step, x from pinned host memory, result back
+    # e2e: host ids planned per step (all layers, one packed upload), x from
+    # pinned host memory, result back
     x_h = torch.from_numpy(x_all0[t0:t1].copy()).pin_memory()
     out_h = torch.empty_like(x_h).pin_memory()
     h2d = [0]
 
     def e2e_step(s):
         x.copy_(x_h, non_blocking=True)
-        pls = []
-        for Lr in range(LAYERS):
-            pl = ep.plan_layer(ids_np[s, Lr], w_np[s, Lr], rank, world, EXPERTS)
-            h2d[0] += pl.tok.nbytes + pl.lid.nbytes + pl.w.nbytes + pl.offsets.nbytes
-            pls.append(ep.plan_to_device(pl))
-        ep.decode_step(x, pls, kops, comm)
+        _, pls = plan_step(s)
+        h2d[0] += pls[0]["_keep"].numel() * 4
+        ep.decode_step(x, pls, kops, comm, exchange)
         out_h.copy_(x, non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -660,13 +670,15 @@ def run_ep(args, rank: int, world: int, local_rank: int):
                    "experts_per_gpu": n_loc, "routing_sets": EP_SETS,
                    "l2": "inputs larger than L2: ~%.1f GB of distinct expert bytes per step over all GPUs"
                          % (totals[0].item() / 1e9),
-                   "parallelism": "ep%d" % world, "exchange": "NCCL all-gather + reduce-scatter per block",
+                   "parallelism": "ep%d" % world,
+                   "exchange": ("NCCL all-gather + reduce-scatter per block" if exchange == "ag" else
+                                "NCCL all-to-all dispatch + combine per block (per-peer row counts)"),
                    "replay": "one CUDA graph per routing set (kernels and collectives)"},
         "roofline": roofline,
         "e2e": {"value": round(EP_TOKENS * 1e3 / e_ms, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x_h.numel() * 4 + h2d[0] / e_steps),
                 "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
-                "path": "ep.decode_step (C ABI kernels + NCCL), host plans per step"},
+                "path": "ep.decode_step (C ABI kernels + NCCL), host plans per step in one packed upload"},
         "gpu_launches": int(launches_per_step * args.steps),
         "clocks": clk,
     }
@@ -1387,6 +1399,8 @@ def main():
                          "cfg2: the headline 1-token decode (replicas for N > 1); cfg3: 512-token prefill "
                          "of one block; cfg4: Q4_K/Q6_K batch-4 decode; cfg5: expert-parallel bank; cfg5s: "
                          "host-resident bank streamed through the hot-tier slab")
+    ap.add_argument("--exchange", default="ag", choices=["ag", "a2a"],
+                    help="cfg5: the expert-parallel exchange (all-gather + reduce-scatter, or all-to-all)")
     ap.add_argument("--source", default="file", choices=["file", "pinned"],
                     help="cfg5s: where the host bank lives (a mapped file, or pinned host memory)")
     ap.add_argument("--layers", type=int, default=LAYERS,

@@ -95,18 +95,19 @@ int sabah_moe_block_gather(const void *gate_bank, const void *up_bank, const voi
 
 /* sabah_moe_block_ids without any allocation. No reference counterpart.
  * sabah_moe_block_ids grows its cross-CTA scratch with cudaMalloc the first
- * time it meets a larger shape, which some callers cannot allow: code being
- * captured into a CUDA graph (an allocation there breaks the capture), a
- * process whose device memory is carved up before serving starts, or a caller
- * holding a lock that an implicit device synchronization could deadlock on.
+ * time it meets a larger shape; this entry point never allocates device or
+ * host memory, for a process whose device memory is carved up before serving
+ * starts, or a caller holding a lock that the implicit device synchronization
+ * of an allocation could deadlock on.
  * IQ3_S gate, up and down only, d_model and ff in {768, 1024, 1536, 2048}.
  * Its scratch is a fixed 1 MiB device array: n_tokens * n_used *
  * (2 * ff + d_model) * 4 bytes must fit in 960 KiB (e.g. 4 tokens x top-10 at
  * 2048/768), else -1 with the limit in sabah_rt_last_error().
- * Set-up: the first call on a device (with that device current) looks up the
- * array's address and queues a clear of its counters on the stream; make that
- * first call before any stream capture. Calls share the array, so calls that
- * overlap on the GPU (two streams, two threads) race and give wrong results. */
+ * Every call queues a clear of the array's arrival counters on its stream
+ * (a memset, no allocation) ahead of its kernels; the first call on a device
+ * (with that device current) also looks up the array's address. Calls share
+ * the array, so calls that overlap on the GPU (two streams, two threads) race
+ * and give wrong results. */
 int sabah_moe_block_ids_noalloc(const void *gate_bank, const void *up_bank, const void *down_bank,
                                 size_t gu_expert_stride, size_t down_expert_stride, int n_experts,
                                 const int32_t *d_ids, const float *d_w, const float *d_x, float *d_out, float *d_h,
@@ -236,6 +237,14 @@ int sabah_ep_sum_rows(const float *d_src, int n_src, const int32_t *d_offsets, i
                       void *stream);
 /* x += y over n floats (n % 4 == 0, 16-byte aligned). Asynchronous. */
 int sabah_ep_add(float *d_x, const float *d_y, long long n, void *stream);
+/* The layer's pair sums with the residual folded in:
+ * dst[t] = (init_row0 <= t < init_row0 + n_init ? init[t - init_row0] : 0)
+ *          + sum over i in [offsets[t], offsets[t + 1]) of src[idx ? idx[i] : i],
+ * in increasing i (deterministic); a source index outside [0, n_src) adds
+ * nothing. init may be dst itself (each element is read before it is
+ * written); src must not overlap dst. Asynchronous. */
+int sabah_ep_sum_rows_ex(const float *d_src, int n_src, const int32_t *d_idx, const int32_t *d_offsets, int n_out,
+                         int k, float *d_dst, const float *d_init, int init_row0, int n_init, void *stream);
 
 #ifdef __cplusplus
 }

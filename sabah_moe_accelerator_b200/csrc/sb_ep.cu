@@ -77,6 +77,47 @@ __global__ void k_sum_rows(const float4* src, int n_src, const int32_t* off, int
     }
 }
 
+// dst[t] = init[t - i0] (t in [i0, i0 + n_init), else 0) + sum over
+// i in [off[t], off[t+1]) of src[idx ? idx[i] : i], in increasing i: the pair
+// sums of a layer with the residual folded in (an index outside [0, n_src)
+// adds nothing). init may alias dst (same element, read before written).
+__global__ void k_sum_rows_ex(const float4* src, int n_src, const int32_t* idx, const int32_t* off, int n_out, int k4,
+                              float4* dst, const float4* init, int i0, int n_init) {
+    const long long total = (long long)n_out * k4;
+    for (long long q = blockIdx.x * (long long)kThreads + threadIdx.x; q < total; q += (long long)gridDim.x * kThreads) {
+        const int t = (int)(q / k4), j = (int)(q % k4);
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (init && t >= i0 && t < i0 + n_init) a = init[(size_t)(t - i0) * k4 + j];
+        const int b0 = __ldg(off + t), b1 = __ldg(off + t + 1);
+        int i = b0;
+        for (; i + 4 <= b1; i += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int r = idx ? __ldg(idx + i + u) : i + u;
+                v[u] = (r >= 0 && r < n_src) ? __ldg(src + (size_t)r * k4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                a.x += v[u].x;
+                a.y += v[u].y;
+                a.z += v[u].z;
+                a.w += v[u].w;
+            }
+        }
+        for (; i < b1; ++i) {
+            const int r = idx ? __ldg(idx + i) : i;
+            if (r < 0 || r >= n_src) continue;
+            const float4 v = __ldg(src + (size_t)r * k4 + j);
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
+        }
+        dst[q] = a;
+    }
+}
+
 // x += y
 __global__ void k_add(float4* x, const float4* y, long long n4) {
     for (long long i = blockIdx.x * (long long)kThreads + threadIdx.x; i < n4; i += (long long)gridDim.x * kThreads) {
@@ -137,4 +178,22 @@ SABAH_API int sabah_ep_add(float* d_x, const float* d_y, long long n, void* stre
     k_add<<<grid_elems(n / 4), kThreads, 0, (cudaStream_t)stream>>>((float4*)d_x, (const float4*)d_y, n / 4);
     sb_timing_end(tslot, (cudaStream_t)stream);
     return sb_cuda_ok(cudaGetLastError(), "ep add launch") ? 0 : -1;
+}
+
+SABAH_API int sabah_ep_sum_rows_ex(const float* d_src, int n_src, const int32_t* d_idx, const int32_t* d_offsets,
+                                   int n_out, int k, float* d_dst, const float* d_init, int init_row0, int n_init,
+                                   void* stream) {
+    if (n_out < 0 || n_src < 0 || k <= 0 || k % 4 || n_init < 0 || (n_out > 0 && (!d_offsets || !d_dst)) ||
+        (n_src > 0 && !d_src) || (n_init > 0 && !d_init) || !aligned16(d_src) || !aligned16(d_dst) ||
+        !aligned16(d_init)) {
+        sb_set_error("invalid ep sum_ex arguments (n_out %d, k %d, n_init %d)", n_out, k, n_init);
+        return -1;
+    }
+    if (n_out == 0) return 0;
+    const int tslot = sb_timing_begin("ep_sum_rows", (cudaStream_t)stream);
+    k_sum_rows_ex<<<grid_elems((long long)n_out * (k / 4)), kThreads, 0, (cudaStream_t)stream>>>(
+        (const float4*)d_src, n_src, d_idx, d_offsets, n_out, k / 4, (float4*)d_dst,
+        n_init > 0 ? (const float4*)d_init : nullptr, init_row0, n_init);
+    sb_timing_end(tslot, (cudaStream_t)stream);
+    return sb_cuda_ok(cudaGetLastError(), "ep sum_ex launch") ? 0 : -1;
 }

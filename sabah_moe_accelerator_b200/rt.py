@@ -113,6 +113,7 @@ SIGNATURES = {
     "sabah_ep_gather_rows": ([c_vp, c_i, c_vp, c_i, c_i, c_vp, c_vp], c_i),
     "sabah_ep_sum_rows": ([c_vp, c_i, c_vp, c_i, c_i, c_vp, c_vp], c_i),
     "sabah_ep_add": ([c_vp, c_vp, ctypes.c_longlong, c_vp], c_i),
+    "sabah_ep_sum_rows_ex": ([c_vp, c_i, c_vp, c_vp, c_i, c_i, c_vp, c_vp, c_i, c_i, c_vp], c_i),
 }
 
 

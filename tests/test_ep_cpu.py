@@ -108,14 +108,15 @@ class _HostOps:
             out[p] = self.cpu.moe_block_f64(g, u, d, [int(lid[p, 0])], [float(w[p, 0])], xp[p].astype(np.float32),
                                             D, F, QT_Q8_0, QT_Q8_0, QT_Q8_0)
 
-    def sum_rows(self, src, offsets, dst):
+    def sum_rows_ex(self, src, n_src, idx, offsets, dst, init, init_row0):
+        n_init = 0 if init is None else init.shape[0]
         for t in range(dst.shape[0]):
-            dst[t] = 0.0
+            acc = init[t - init_row0].copy() if init_row0 <= t < init_row0 + n_init else np.zeros(D)
             for i in range(offsets[t], offsets[t + 1]):
-                dst[t] += src[i]
-
-    def add(self, x, y):
-        x += y
+                r = i if idx is None else int(idx[i])
+                if 0 <= r < n_src:
+                    acc += src[r]
+            dst[t] = acc
 
 
 class _HostOpsRows(_HostOps):
@@ -138,15 +139,27 @@ class _GlooComm:
         self.dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(x_own)))
         return torch.cat(parts).numpy()
 
-    def reduce_scatter(self, y):
+    def reduce_scatter(self, y, out=None):
         import torch
         t = torch.from_numpy(np.ascontiguousarray(y))
         self.dist.all_reduce(t)
         n = y.shape[0] // self.world
-        return t.numpy()[self.rank * n:(self.rank + 1) * n].copy()
+        part = t.numpy()[self.rank * n:(self.rank + 1) * n]
+        if out is None:
+            return part.copy()
+        out[:] = part
+        return out
+
+    def all_to_all(self, send, send_splits, recv, recv_splits):
+        import torch
+        r = torch.empty((recv.shape[0], D), dtype=torch.float64)
+        self.dist.all_to_all_single(r, torch.from_numpy(np.ascontiguousarray(send)).reshape(-1, D),
+                                    output_split_sizes=list(recv_splits), input_split_sizes=list(send_splits))
+        recv[:] = r.numpy()
+        return recv
 
 
-def _rank_main(rank, world, port, out_path, rows_mode=False):
+def _rank_main(rank, world, port, out_path, rows_mode=False, exchange="ag"):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -157,13 +170,24 @@ def _rank_main(rank, world, port, out_path, rows_mode=False):
         local = [(g[e0:e1], u[e0:e1], d[e0:e1]) for g, u, d in banks]
         plans = []
         for L in range(LAYERS):
-            pl = ep.plan_layer(ids[L], w[L], rank, world, E)
-            plans.append({"n_pairs": pl.n_pairs, "tok": pl.tok, "lid": pl.lid.reshape(-1, 1),
-                          "w": pl.w.reshape(-1, 1), "offsets": pl.offsets})
+            if exchange == "ag":
+                pl = ep.plan_layer(ids[L], w[L], rank, world, E)
+                perm, pos = ep.expert_order(pl.lid)
+                plans.append({"n_pairs": pl.n_pairs, "tok": pl.tok[perm], "lid": pl.lid[perm].reshape(-1, 1),
+                              "w": pl.w[perm].reshape(-1, 1), "offsets": pl.offsets, "sum_idx": pos})
+            else:
+                pl = ep.plan_layer_a2a(ids[L], w[L], rank, world, E)
+                perm, pos = ep.expert_order(pl.lid)
+                plans.append({"n_pairs": pl.n_pairs, "n_send": sum(pl.send_splits), "n_recv": sum(pl.recv_splits),
+                              "send_splits": pl.send_splits, "recv_splits": pl.recv_splits,
+                              "send_rows": pl.send_rows, "pair_row": pl.pair_row[perm],
+                              "lid": pl.lid[perm].reshape(-1, 1), "w": pl.w[perm].reshape(-1, 1),
+                              "pair_off": pl.pair_off, "pair_sum_idx": pos, "comb_idx": pl.comb_idx,
+                              "comb_off": pl.comb_off})
         t0, t1 = ep.token_range(rank, T, world)
         x_own = x0[t0:t1].copy()
         ops = _HostOpsRows(local) if rows_mode else _HostOps(local)
-        ep.decode_step(x_own, plans, ops, _GlooComm())
+        ep.decode_step(x_own, plans, ops, _GlooComm(), exchange)
         np.save(out_path % rank, x_own)
     finally:
         dist.destroy_process_group()
@@ -175,12 +199,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("rows_mode", [False, True])
-def test_gloo_two_ranks_match_single_process_chain(tmp_path, orc, rows_mode):
+@pytest.mark.parametrize("rows_mode,exchange,world", [(False, "ag", 2), (True, "ag", 2), (False, "a2a", 2),
+                                                      (True, "a2a", 2), (True, "a2a", 4), (True, "ag", 4)])
+def test_gloo_ranks_match_single_process_chain(tmp_path, orc, rows_mode, exchange, world):
     import torch.multiprocessing as mp
-    world = 2
     out = str(tmp_path / "x_%d.npy")
-    mp.start_processes(_rank_main, args=(world, _free_port(), out, rows_mode), nprocs=world, start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, _free_port(), out, rows_mode, exchange), nprocs=world,
+                       start_method="spawn")
     got = np.concatenate([np.load(out % r) for r in range(world)])
 
     banks, ids, w, x0 = _problem()
@@ -191,3 +216,43 @@ def test_gloo_two_ranks_match_single_process_chain(tmp_path, orc, rows_mode):
                                                      QT_Q8_0, QT_Q8_0, QT_Q8_0) for t in range(T)])
     # fp64 sums in another order; x enters each block as fp32, as in the kernels
     assert orc.rel_l2(got, want) < 1e-6
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_a2a_plan_routes_every_pair_once(world):
+    """The all-to-all plans of all ranks: every (token, slot) is computed on its
+    expert's owner exactly once, on a row that carries that token, and every
+    partial goes back to the token's owner exactly once per peer it visited."""
+    rng = np.random.default_rng(100 + world)
+    T_, K_, E_ = 64, 10, 512
+    ids = np.stack([rng.choice(E_, K_, replace=False) for _ in range(T_)]).astype(np.int32)
+    w = rng.random((T_, K_)).astype(np.float32)
+    plans = [ep.plan_layer_a2a(ids, w, r, world, E_) for r in range(world)]
+    seen = np.zeros((T_, K_), np.int32)
+    for r, pl in enumerate(plans):
+        assert sum(pl.send_splits) == pl.send_rows.size and sum(pl.recv_splits) == pl.pair_off.size - 1
+        e0, e1 = ep.expert_range(r, E_, world)
+        # the rows r receives, in the senders' order
+        recv_tok = []
+        for src in range(world):
+            s0, _ = ep.token_range(src, T_, world)
+            spl = plans[src].send_splits
+            b = sum(spl[:r])
+            recv_tok += list(s0 + plans[src].send_rows[b:b + spl[r]])
+            assert spl[r] == pl.recv_splits[src]
+        for j, t in enumerate(recv_tok):
+            sl = slice(pl.pair_off[j], pl.pair_off[j + 1])
+            assert np.all(pl.pair_row[sl] == j)
+            ks = [k for k in range(K_) if e0 <= ids[t, k] < e1]
+            assert list(pl.lid[sl] + e0) == [int(ids[t, k]) for k in ks] and np.array_equal(pl.w[sl], w[t, ks])
+            seen[t, ks] += 1
+        # combine: token i of r gets one partial from each peer that hosts one of its slots
+        t0, t1 = ep.token_range(r, T_, world)
+        for i in range(t1 - t0):
+            got = pl.comb_idx[pl.comb_off[i]:pl.comb_off[i + 1]]
+            peers = sorted({int(e) * world // E_ for e in ids[t0 + i]})
+            assert len(got) == len(peers) and np.all(np.diff(got) > 0)
+            base = np.concatenate([[0], np.cumsum(pl.send_splits)])
+            for g_, d in zip(got, peers):
+                assert base[d] <= g_ < base[d + 1] and pl.send_rows[g_] == i
+    assert np.all(seen == 1)

@@ -61,12 +61,16 @@ def _single_gpu_reference(banks, ids, w, x0):
     return x.cpu().numpy()
 
 
-def test_ep_world1_matches_decode_and_fp64(gpu_rt, orc):
+@pytest.mark.parametrize("exchange", ["ag", "a2a"])
+def test_ep_world1_matches_decode_and_fp64(gpu_rt, orc, exchange):
     from sabah_moe_accelerator_b200 import ep
     banks, ids, w, x0 = problem()
-    plans = [ep.plan_to_device(ep.plan_layer(ids[L], w[L], 0, 1, E)) for L in range(LAYERS)]
+    if exchange == "ag":
+        plans = ep.pack_plans([ep.plan_layer(ids[L], w[L], 0, 1, E) for L in range(LAYERS)])
+    else:
+        plans = ep.pack_plans_a2a([ep.plan_layer_a2a(ids[L], w[L], 0, 1, E) for L in range(LAYERS)])
     x = torch.from_numpy(x0).cuda()
-    ep.decode_step(x, plans, ep.CudaOps(banks, D, F, E, QT), ep.SingleComm())
+    ep.decode_step(x, plans, ep.CudaOps(banks, D, F, E, QT), ep.SingleComm(), exchange)
     torch.cuda.synchronize()
     got = x.cpu().numpy()
     assert gpu_rt.sabah_rt_device_error() == 0
@@ -97,6 +101,27 @@ def test_ep_sum_rows_and_gather_edges(gpu_rt):
     assert torch.equal(dst[0], src[1]) and float(dst[1:].abs().sum()) == 0.0
 
 
+def test_ep_sum_rows_ex_residual_and_index(gpu_rt):
+    """The fused pair sum: residual rows folded in (in place, or at a row
+    offset), indexed sources, out-of-range indices add nothing."""
+    from sabah_moe_accelerator_b200 import ep
+    ops_ = ep.CudaOps([], D, F, E, QT)
+    src = torch.randn(5, D, device="cuda")
+    x = torch.randn(3, D, device="cuda")
+    idx = torch.tensor([4, 0, 9, 2, -1], dtype=torch.int32, device="cuda")
+    off = torch.tensor([0, 2, 2, 5], dtype=torch.int32, device="cuda")
+    dst = x.clone()
+    ops_.sum_rows_ex(src, 5, idx, off, dst, dst, 0)
+    x1 = torch.randn(1, D, device="cuda")
+    dst2 = torch.full((3, D), 9.0, device="cuda")
+    ops_.sum_rows_ex(src, 5, None, torch.tensor([0, 1, 3, 5], dtype=torch.int32, device="cuda"), dst2, x1, 1)
+    torch.cuda.synchronize()
+    assert torch.allclose(dst[0], x[0] + src[4] + src[0]) and torch.equal(dst[1], x[1])
+    assert torch.allclose(dst[2], x[2] + src[2])
+    assert torch.allclose(dst2[0], src[0]) and torch.allclose(dst2[1], x1[0] + src[1] + src[2])
+    assert torch.allclose(dst2[2], src[3] + src[4])
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -104,11 +129,13 @@ def _free_port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_ep_two_ranks_match_single_gpu(gpu_rt, tmp_path):
+@pytest.mark.parametrize("exchange", ["ag", "a2a"])
+def test_ep_two_ranks_match_single_gpu(gpu_rt, tmp_path, exchange):
     out = str(tmp_path / "ep")
     env = dict(os.environ, PYTHONPATH=HERE + os.pathsep + os.path.dirname(HERE))
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=%d" % _free_port(), os.path.join(HERE, "ep_child.py"), out]
+           "--master-addr=127.0.0.1", "--master-port=%d" % _free_port(), os.path.join(HERE, "ep_child.py"), out,
+           exchange]
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     got = np.concatenate([np.load("%s_%d.npy" % (out, k)) for k in range(2)])

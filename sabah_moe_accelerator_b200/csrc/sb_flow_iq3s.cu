@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
         // h = silu(g) * u; every use: releases the stage to the producer. After
         // the down stages of a layer: the unit's combine, x_{L+1} = x_L + y.
         consumers_sync();
-        // lane (hf, r): row r; half hf of the row's partials
+        // lane (hf, r): row r; half hf of the row's gate/up partials
         const int r = lane & 15, hf = lane >> 4;
         const int row = cta * 16 + r;
         const int spr = p.Gd / 2;   // super-blocks per down row
@@ -415,9 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 }
             }
             if (!ok || nd == 0) continue;
-            // every task of the unit is done: y_r = sum over tasks of w(slot) *
-            // partial, in a fixed order; half hf takes tasks [16 hf, 16 hf + 16)
-            // of every 32
+            // every task of the unit is done: super-blocks in order, slots in order (weighted)
             float tot = 0.f;
             for (int e2 = 0; e2 < p.n_used; ++e2) {
                 float v = 0.f;
@@ -425,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 tot += __shfl_sync(0xffffffffu, wl, e2) * v;
             }
             xr = xr + tot;
-            __syncwarp();   // dred and wt are read before the next layer writes them
+            __syncwarp();   // dred is read before the next layer's tasks may write it
             if (lane < 16) {
                 if (L + 1 < p.n_layers)
                     st_pair(p.xpairs + (size_t)((L + 1) & 1) * p.d_model + row, xr, tag + 1u);

@@ -646,7 +646,7 @@ __global__ void k_x_split(const uint8_t* x, size_t x_id_stride, size_t x_token_s
 constexpr int kGW = 8;                       // consumer warps (16 rows each: one 128-row block)
 constexpr int kGThreads = (kGW + 1) * 32;    // + the producer warp
 constexpr int kGTile = 16 * 880;             // a 16-row tile at k <= 2048
-constexpr int kGRep = 8;                     // grid-table replicas
+constexpr int kGRep = 16;                    // grid-table replicas (lane % 16: at most 2-way bank conflicts)
 constexpr int kGXRow = 2048 * 2 + 32;        // bytes per staged x row (fp16, padded against bank conflicts)
 
 struct MmaSmem {
@@ -777,44 +777,59 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
         if (!__all_sync(0xffffffffu, ok)) break;
         const bool have = g < t.n;   // pair column g exists (else its B is zero)
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int sb = 0; sb < p.k / 32; ++sb) {
-            const int j = sb >> 3, ib = sb & 7;
-            uint32_t a[2][2][2];   // [k16 half q][row h][reg]
-            float db[2];
+        // super-block by super-block: its scale d and 4 scale bytes are read
+        // once, and its 8 sub-blocks are unrolled so their loads, lookups and
+        // MMAs overlap (the kernel runs 9 warps per SM, so a warp needs
+        // independent work of its own to hide latency)
+        for (int j = 0; j < p.k / 256; ++j) {
+            float d[2];
+            uint32_t scw[2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint8_t* rb = tile + (size_t)(g + 8 * h) * p.rb + j * 110;
-                const float d = __half2float(__ushort_as_half(*(const unsigned short*)rb));
-                const unsigned nib = (rb[106 + (ib >> 1)] >> (4 * (ib & 1))) & 15u;
-                db[h] = d * (float)(1 + 2 * (int)nib) * 16777216.f;   // 2^24 undoes the subnormal encoding
-                const unsigned qh = rb[66 + ib];
+                d[h] = __half2float(__ushort_as_half(*(const unsigned short*)rb)) * 16777216.f;   // 2^24: subnormal encoding
+                scw[h] = (uint32_t)rb[106] | ((uint32_t)rb[107] << 8) | ((uint32_t)rb[108] << 16) |
+                         ((uint32_t)rb[109] << 24);
+            }
+#pragma unroll
+            for (int ib = 0; ib < 8; ++ib) {
+                const int sb = 8 * j + ib;
+                uint32_t a[2][2][2];   // [k16 half q][row h][reg]
+                float db[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint8_t* rb = tile + (size_t)(g + 8 * h) * p.rb + j * 110;
+                    const unsigned nib = (scw[h] >> (4 * ib)) & 15u;
+                    db[h] = d[h] * (float)(1 + 2 * (int)nib);
+                    const unsigned qh = rb[66 + ib];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int e = 4 * q + c;
+                        const uint32_t idx = rb[2 + 8 * ib + e] | (((qh >> e) & 1u) << 8);
+                        const uint32_t gw = gtab[idx * kGRep + grep];
+                        const uint32_t sg = (rb[74 + 4 * ib + (e >> 1)] >> (4 * (e & 1))) & 15u;
+                        const uint32_t Z = (sg * 0x10204080u) & 0x80808080u;   // sign bit i -> bit 7 of byte i
+                        a[q][h][0] = prmt(gw, Z, 0x5140);   // (w0, w1) as signed fp16 subnormals
+                        a[q][h][1] = prmt(gw, Z, 0x7362);   // (w2, w3)
+                    }
+                }
+                float dd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
-                    const int e = 4 * q + c;
-                    const uint32_t idx = rb[2 + 8 * ib + e] | (((qh >> e) & 1u) << 8);
-                    const uint32_t gw = gtab[idx * kGRep + grep];
-                    const uint32_t sg = (rb[74 + 4 * ib + (e >> 1)] >> (4 * (e & 1))) & 15u;
-                    const uint32_t Z = (sg * 0x10204080u) & 0x80808080u;   // sign bit i -> bit 7 of byte i
-                    a[q][h][0] = prmt(gw, Z, 0x5140);   // (w0, w1) as signed fp16 subnormals
-                    a[q][h][1] = prmt(gw, Z, 0x7362);   // (w2, w3)
+                    const int off = 2 * (32 * sb + 16 * q + 4 * c);
+                    uint2 bh = make_uint2(0, 0), bl = make_uint2(0, 0);
+                    if (have) {
+                        bh = *(const uint2*)(xhs + off);
+                        bl = *(const uint2*)(xls + off);
+                    }
+                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bh.x, bh.y);
+                    mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bl.x, bl.y);
                 }
+                acc[0] = fmaf(db[0], dd[0], acc[0]);
+                acc[1] = fmaf(db[0], dd[1], acc[1]);
+                acc[2] = fmaf(db[1], dd[2], acc[2]);
+                acc[3] = fmaf(db[1], dd[3], acc[3]);
             }
-            float dd[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int off = 2 * (32 * sb + 16 * q + 4 * c);
-                uint2 bh = make_uint2(0, 0), bl = make_uint2(0, 0);
-                if (have) {
-                    bh = *(const uint2*)(xhs + off);
-                    bl = *(const uint2*)(xls + off);
-                }
-                mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bh.x, bh.y);
-                mma16816(dd, a[q][0][0], a[q][1][0], a[q][0][1], a[q][1][1], bl.x, bl.y);
-            }
-            acc[0] = fmaf(db[0], dd[0], acc[0]);
-            acc[1] = fmaf(db[0], dd[1], acc[1]);
-            acc[2] = fmaf(db[1], dd[2], acc[2]);
-            acc[3] = fmaf(db[1], dd[3], acc[3]);
         }
         // D: (row g, pair 2c), (row g, pair 2c + 1), (row g + 8, pair 2c), (row g + 8, pair 2c + 1)
         const int row0 = (t.mt * kGW + warp) * 16;

@@ -304,9 +304,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_prefill_iq3s(const GemmParams p
     } else {
         // ---------------------------------------------------------- producers (warps 0-7)
         // every producer thread does both jobs each slice:
-        //   A: row r = tid % 128, entries 4h .. 4h + 3 (h = tid / 128) of the slice's sub-block
+        //   A: rows r1 = 16 warp + (lane & 7) and r1 + 8, quarter aq = lane / 8 of the
+        //      slice's sub-block (entries 2 aq, 2 aq + 1: weights 8 aq .. + 7). A warp's
+        //      32 lanes then read 8 rows x 4 column words: rows 880 B apart sit 4 banks
+        //      apart, the quarters 1 bank apart, so the raw-tile loads are conflict-free
         //   B: (pair column, 8-wide chunk) jobs q = tid and tid + 256 of the slice (n_pad x 4 jobs)
-        const int r = tid & (kM - 1), h = tid >> 7;
+        const int aq = lane >> 3, r1 = 16 * warp + (lane & 7);
+        const int arow[2] = {r1, r1 + 8};
         const uint32_t grep = (uint32_t)(lane & (kGridReplicas - 1));
         const uint8_t* raw = smem + Smem::raw;
         int g = 0, i = 0;
@@ -317,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_prefill_iq3s(const GemmParams p
                 const Task tn = p.tasks[ti + gridDim.x];
                 prefetch_l2(p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * kM * p.rb, tile_bytes);
             }
-            const uint8_t* rowp = raw + (size_t)r * p.rb;
+            const uint8_t* rowp[2] = {raw + (size_t)arow[0] * p.rb, raw + (size_t)arow[1] * p.rb};
             // pair tables of the task (epilogue) and this thread's B jobs
             if (tid < nn) {
                 const PairInfo pi = p.pairs[t.n0 + tid];
@@ -342,21 +346,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_prefill_iq3s(const GemmParams p
             }
             mbar_wait(rawbar, i & 1, p.err, abort_flag);   // on failure the abort flag is read below
             if (tid == 0) ++raw_waited;
-            if (h == 0) {
+            if (aq == 0) {
                 // row scale: |w| <= |d| * 31 * 15 per super-block
-                float m = 0.f;
-                for (int j = 0; j < p.k / 256; ++j) m = fmaxf(m, fabsf(f16_bits(*(const unsigned short*)(rowp + j * 110))));
-                m *= 465.f;
-                int ex = 0;
-                if (m > 0.f && isfinite(m)) {
-                    frexpf(m, &ex);
-                    ex = max(-100, min(100, 14 - ex));
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    float m = 0.f;
+                    for (int j = 0; j < p.k / 256; ++j)
+                        m = fmaxf(m, fabsf(f16_bits(*(const unsigned short*)(rowp[u] + j * 110))));
+                    m *= 465.f;
+                    int ex = 0;
+                    if (m > 0.f && isfinite(m)) {
+                        frexpf(m, &ex);
+                        ex = max(-100, min(100, 14 - ex));
+                    }
+                    row_exp[arow[u]] = ex;
                 }
-                row_exp[r] = ex;
             }
             producers_sync();   // row scales written; a uniform decision on the abort flag
             if (*abort_flag) break;
-            const float rs = ldexpf(1.f, row_exp[r]);
+            const float rs[2] = {ldexpf(1.f, row_exp[arow[0]]), ldexpf(1.f, row_exp[arow[1]])};
             // B: the next slice's x is loaded while the current one is converted
             float4 xn[2][2];
 #pragma unroll
@@ -373,16 +381,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_prefill_iq3s(const GemmParams p
                     if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
                 }
                 uint8_t* st = smem + Smem::stage + s * kStageBytes;
-                {   // A: 16 weights (entries 4h .. 4h + 3) of sub-block kt of row r
+                {   // A: weights 8 aq .. 8 aq + 7 (entries 2 aq, 2 aq + 1) of sub-block kt of rows arow[]
                     const int j = kt >> 3, ib = kt & 7;
-                    const uint8_t* bb = rowp + j * 110;
-                    const unsigned sc = (bb[106 + (ib >> 1)] >> (4 * (ib & 1))) & 15;
-                    const float db = f16_bits(*(const unsigned short*)bb) * (float)(1 + 2 * sc) * rs;
-                    const float dbc = -8388608.f * db;   // byte b -> float(2^23 + b) * db - 2^23 * db = b * db
-                    const unsigned qh = bb[66 + ib];
 #pragma unroll
-                    for (int c2 = 0; c2 < 2; ++c2) {       // entries 4h + 2c2, + 1: weights 16h + 8c2 .. + 7
-                        const int c = 2 * h + c2;
+                    for (int u = 0; u < 2; ++u) {
+                        const uint8_t* bb = rowp[u] + j * 110;
+                        const unsigned sc = (bb[106 + (ib >> 1)] >> (4 * (ib & 1))) & 15;
+                        const float db = f16_bits(*(const unsigned short*)bb) * (float)(1 + 2 * sc) * rs[u];
+                        const float dbc = -8388608.f * db;   // byte b -> float(2^23 + b) * db - 2^23 * db = b * db
+                        const unsigned qh = bb[66 + ib];
+                        const int c = aq;
+                        const int r = arow[u];
                         const unsigned qs2 = *(const unsigned short*)(bb + 2 + 8 * ib + 2 * c);
                         const unsigned sg = bb[74 + 4 * ib + c];
                         float v[8];

@@ -260,9 +260,40 @@ struct Fetch {
     size_t bytes;
     int expert;
     uint64_t shape;
+    const void* src_key;   // the tensor the slot belongs to
 };
 
+// ---------------------------- call chain (merged layer fetch) ----------------
+// A forward pass issues the same MUL_MAT_ID calls in the same order, and a
+// layer's gate, up and down tensors read the same router ids. Each host-source
+// call records which tensor followed which, and whether they shared the ids
+// (ref sabah_rt.cu:1870-1943, sb_chain_note). With SABAH_LLAMA_LAYER_MERGE=1
+// the first call of a layer also reserves and fills its followers' missing
+// experts in its own fill wave (ref :1944-2000), so the layer's reads go out
+// together and the followers' calls find their experts resident. Off by
+// default, as in the reference: the followers' memory must stay mapped, which
+// a GGUF mapping does and an arbitrary caller's buffer may not.
+struct ChainLink {
+    const void* next = nullptr;
+    size_t stride = 0;
+    uint64_t shape = 0;
+    int n_experts = 0;
+    bool shares_ids = false;
+};
+struct Chain {
+    std::unordered_map<const void*, ChainLink> links;
+    const void* prev = nullptr;
+    std::vector<int32_t> prev_ids;
+    uint64_t merged_slots = 0;   // follower slots filled in an earlier call's wave
+} g_chain;
+
+bool layer_merge_enabled() {
+    const char* v = std::getenv("SABAH_LLAMA_LAYER_MERGE");
+    return v && (!std::strcmp(v, "1") || !std::strcmp(v, "on"));
+}
+
 void residency_reset_locked() {
+    g_chain = Chain{};
     for (auto& kv : g_res.map) {
         if (kv.second.slab) {
             std::lock_guard<std::mutex> ls(g_slab.mu);
@@ -382,12 +413,12 @@ void* slot_locked(const void* src_key, int expert, const void* src, size_t bytes
     g_res.map.emplace(key, e);
     g_res.bytes += bytes;
     g_res.bytes_fetched += bytes;
-    miss.push_back({src, dev, bytes, expert, shape});
+    miss.push_back({src, dev, bytes, expert, shape, src_key});
     return dev;
 }
 
 // Copy every reserved slot in from the host on the copy stream.
-bool fill_locked(const std::vector<Fetch>& miss, const std::set<uint64_t>& wait_epochs, const void* src_key) {
+bool fill_locked(const std::vector<Fetch>& miss, const std::set<uint64_t>& wait_epochs) {
     for (uint64_t ep : wait_epochs) {
         const int r = (int)(ep % kEventRing);
         if (g_res.done[r] && g_res.done_epoch[r] == ep &&
@@ -401,7 +432,7 @@ bool fill_locked(const std::vector<Fetch>& miss, const std::set<uint64_t>& wait_
     for (const Fetch& f : miss) fills.push_back({f.dst, f.src, f.bytes});
     if (!fills.empty() && !sb_stage_fill(fills.data(), (int)fills.size(), g_rt.copy)) return false;
     for (const Fetch& f : miss) {
-        auto it = g_res.map.find(Key{src_key, f.expert, f.bytes, f.shape});
+        auto it = g_res.map.find(Key{f.src_key, f.expert, f.bytes, f.shape});
         if (it != g_res.map.end()) it->second.filled = true;
         if (g_res.verify) {
             if (!sb_cuda_ok(cudaStreamSynchronize(g_rt.copy), "verify sync")) return false;
@@ -612,7 +643,7 @@ int snapshot_json(char* buf, size_t n) {
         "\"selfcheck_multi_token\":%llu,\"selfcheck_tensors\":%llu,\"selfcheck_slots\":[%s],"
         "\"sentinel\":%d,\"device_calls\":%llu,\"id_reuse\":%llu,"
         "\"staged_bytes\":%llu,\"pinned_fill_bytes\":%llu,\"direct_io_reads\":%llu,\"direct_io_bytes\":%llu,"
-        "\"direct_io_fallbacks\":%llu,\"fill_waves\":%llu}",
+        "\"direct_io_fallbacks\":%llu,\"fill_waves\":%llu,\"merged_slots\":%llu}",
         (unsigned long long)g_res.calls, (unsigned long long)g_res.empty_calls, (unsigned long long)g_res.tokens,
         (unsigned long long)(g_res.hits + g_res.misses), (unsigned long long)g_res.hits,
         (unsigned long long)g_res.misses, (unsigned long long)g_res.evictions,
@@ -622,7 +653,8 @@ int snapshot_json(char* buf, size_t n) {
         (unsigned long long)g_res.sc_fail, g_res.sc_max, (unsigned long long)g_res.sc_multi_token,
         (unsigned long long)g_res.sc_tensors.size(), slots, SABAH_SENTINEL,
         (unsigned long long)g_res.device_calls, (unsigned long long)g_res.id_reuse, ss.staged_bytes, ss.pinned_bytes,
-        ss.direct_io_reads, ss.direct_io_bytes, ss.direct_io_fallbacks, ss.waves);
+        ss.direct_io_reads, ss.direct_io_bytes, ss.direct_io_fallbacks, ss.waves,
+        (unsigned long long)g_chain.merged_slots);
 }
 
 void status_write() {
@@ -1237,7 +1269,41 @@ SABAH_API int sabah_rt_mul_mat_id_v2(const void* source, size_t expert_stride, s
                 ptrs[(size_t)t * n_ids + i] = d;
             }
         }
-        if (!fill_locked(miss, wait_epochs, source)) return -1;
+        // learn the call chain: close the previous call's edge, then, when
+        // merging, reserve the followers' experts in this call's wave
+        std::vector<int32_t> ids_now((size_t)n_slots);
+        for (int t = 0; t < n_tokens; ++t)
+            for (int i = 0; i < n_ids; ++i)
+                ids_now[(size_t)t * n_ids + i] =
+                    *(const int32_t*)(ids_raw + (size_t)t * ids_token_stride + (size_t)i * ids_id_stride);
+        if (g_chain.prev && g_chain.prev != source) {
+            ChainLink& l = g_chain.links[g_chain.prev];
+            l.next = source;
+            l.stride = expert_stride;
+            l.shape = shape;
+            l.n_experts = n_experts;
+            l.shares_ids = g_chain.prev_ids == ids_now;
+        }
+        if (layer_merge_enabled()) {
+            const void* f = source;
+            for (int depth = 0; depth < 2; ++depth) {   // the layer's up to two followers
+                auto li = g_chain.links.find(f);
+                if (li == g_chain.links.end() || !li->second.shares_ids || !li->second.next) break;
+                const ChainLink l = li->second;
+                for (int32_t e : ids_now) {
+                    if (e < 0 || e >= l.n_experts) continue;
+                    const size_t before = miss.size();
+                    if (!slot_locked(l.next, e, (const uint8_t*)l.next + (size_t)e * l.stride, l.stride, l.shape, miss,
+                                     wait_epochs))
+                        return -1;
+                    g_chain.merged_slots += miss.size() - before;
+                }
+                f = l.next;
+            }
+        }
+        g_chain.prev = source;
+        g_chain.prev_ids.swap(ids_now);
+        if (!fill_locked(miss, wait_epochs)) return -1;
     }
     void** d_ptrs = nullptr;
     if (!ptr_table(n_slots * sizeof(void*), &d_ptrs)) return -1;

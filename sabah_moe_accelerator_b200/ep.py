@@ -133,22 +133,16 @@ def plan_layer_a2a(ids: np.ndarray, w: np.ndarray, rank: int, world: int, n_expe
     if T % world:
         raise ValueError("the token count must be a multiple of the world size")
     owner = (ids.astype(np.int64) * world) // n_experts          # [T][K] owner rank of each slot
-    hits = np.stack([(owner == d).any(1) for d in range(world)])  # [world][T]: token t has a slot on d
+    hits = np.zeros((world, T), bool)                             # [world][T]: token t has a slot on d
+    hits[owner, np.arange(T)[:, None]] = True
     t0, t1 = token_range(rank, T, world)
-    # dispatch: owned tokens needed by each peer
-    send_rows, send_splits = [], []
-    for d in range(world):
-        tt = np.nonzero(hits[d, t0:t1])[0]
-        send_rows.append(tt)
-        send_splits.append(int(tt.size))
-    # receive: each peer's tokens that have a slot here, then the local pairs
-    recv_tok, recv_splits = [], []
-    for src in range(world):
-        s0, s1 = token_range(src, T, world)
-        tt = s0 + np.nonzero(hits[rank, s0:s1])[0]
-        recv_tok.append(tt)
-        recv_splits.append(int(tt.size))
-    recv_tok = np.concatenate(recv_tok) if recv_tok else np.zeros(0, np.int64)
+    # dispatch: owned tokens needed by each peer, peer by peer, token order within
+    own = hits[:, t0:t1]
+    send_splits = own.sum(1).astype(np.int64).tolist()
+    send_rows = np.nonzero(own)[1].astype(np.int32)
+    # receive: every token with a slot here, in token order, which is peer order
+    recv_tok = np.nonzero(hits[rank])[0]
+    recv_splits = np.bincount(recv_tok // (T // world), minlength=world).astype(np.int64).tolist()
     mine = owner[recv_tok] == rank                                # [R][K]
     j_idx, k_idx = np.nonzero(mine)                               # by received row, then slot
     pair_off = np.zeros(recv_tok.size + 1, np.int32)
@@ -156,17 +150,15 @@ def plan_layer_a2a(ids: np.ndarray, w: np.ndarray, rank: int, world: int, n_expe
     e0, _ = expert_range(rank, n_experts, world)
     toks = recv_tok[j_idx]
     # combine: owned token i's partials sit in the combine buffer at the rows
-    # where send_rows put it, peer by peer
-    base = np.concatenate([[0], np.cumsum(send_splits)]).astype(np.int64)
-    comb = [[] for _ in range(t1 - t0)]
-    for d in range(world):
-        for pos, i in enumerate(send_rows[d]):
-            comb[i].append(base[d] + pos)
+    # where send_rows put it, peer by peer (row of (d, i) = start of peer d's
+    # block + rank of i among the tokens sent to d)
+    base = np.concatenate([[0], np.cumsum(send_splits)])[:world].astype(np.int64)
+    row_of = base[:, None] + np.cumsum(own, axis=1) - 1
+    mask_t = own.T                                                # [n_own][world], peer order per token
+    comb_idx = row_of.T[mask_t].astype(np.int32)
     comb_off = np.zeros(t1 - t0 + 1, np.int32)
-    np.cumsum([len(c) for c in comb], out=comb_off[1:])
-    comb_idx = np.array([r for c in comb for r in c], np.int32)
-    return A2APlan(send_rows=np.concatenate(send_rows).astype(np.int32) if send_rows else np.zeros(0, np.int32),
-                   send_splits=send_splits, recv_splits=recv_splits, pair_row=j_idx.astype(np.int32),
+    np.cumsum(mask_t.sum(1), out=comb_off[1:])
+    return A2APlan(send_rows=send_rows, send_splits=send_splits, recv_splits=recv_splits, pair_row=j_idx.astype(np.int32),
                    lid=(ids[toks, k_idx] - e0).astype(np.int32), w=w[toks, k_idx].astype(np.float32),
                    pair_off=pair_off, comb_idx=comb_idx, comb_off=comb_off)
 

@@ -14,20 +14,23 @@
 //   no barrier. Tags are (epoch << 6) + L + 1; the epoch word is bumped by the
 //   last CTA to exit, so a CUDA-graph replay never mistakes an earlier
 //   launch's pairs for its own. x and h are double-buffered by layer parity.
-// * Work is balanced on the warp: a gate/up item is 8 gate rows and the same 8
-//   up rows of one slot (a stacked 16-row MMA tile) over the full row; items go
-//   round-robin over the CTAs (n_used * ff / 8 = 960 items on 148 CTAs), and
-//   consumer warp w takes group w (128 weights) of every item, so each warp does
-//   exactly the CTA's item count of groups. The item's last warp sums the 16
-//   warps' partial rows in fixed order and publishes h = silu(g) * u.
-//   Round-robin order finishes slot 0 first, so down work can start on it
-//   while later slots are still in flight.
-// * A down unit is 16 output rows over all n_used slots (d_model / 16 = 128
-//   units, one per CTA); its tasks (slot, group) go round-robin over the
-//   warps. A task needs only its own 128 values of h: the warp polls those
-//   pairs, converts them to the B fragments of mma.sync in registers, and runs.
-//   The unit's last task sums the partial rows (groups in order, then slots in
-//   order, weighted) and publishes x_{L+1} = x_L + y.
+// * A gate/up item is 8 gate rows and the same 8 up rows of one slot (a
+//   stacked 16-row MMA tile) over the full row. Consumer warp w decodes group
+//   w (128 weights) of every item of its CTA, two items at a time (two MMA
+//   chains sharing the B fragments), so each warp does the CTA's item count of
+//   groups. Items are handed out in rounds (round k: the k-th item of every
+//   CTA) and numbered in slot order, so early slots finish in the first rounds
+//   everywhere. The epilogue warp sums an item's 16 warp partials in fixed
+//   order and publishes h = silu(g) * u.
+// * A down unit is 16 output rows over all n_used slots, one per CTA (d_model
+//   / 16 = 128 units). Its tasks (slot, super-block) go round-robin over the
+//   warps, in slot order. A task needs only its own 256 values of h: the warp
+//   polls those pairs (requested during its previous task), stages them as B
+//   fragments and decodes one super-block. After the layer's down stages the
+//   epilogue sums the unit's task partials (super-blocks in order, then slots
+//   in order, weighted) and publishes x_{L+1} = x_L + y.
+// * The CTAs without a unit take more gate/up items, so that a unit CTA's
+//   gate/up plus down work matches the others' gate/up work.
 // * In gate/up, warp w's B fragments (group w of x) are built once per layer
 //   and kept in registers for all its items.
 // * Weights are inputs, so the producer warp streams tiles of the next items

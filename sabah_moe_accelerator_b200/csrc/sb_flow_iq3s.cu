@@ -36,8 +36,9 @@
 // * Weights are inputs, so the producer warp streams tiles of the next items
 //   (next layers included) while consumers wait for data.
 //
-// The decode core (grid lookup + PRMT into fp16 subnormals + mma.sync with x
-// in fp16 hi/lo parts, scale per sub-block) is the one of sb_iq3s_core.cuh.
+// The decode core (grid lookup into fp16 subnormals with their signs +
+// mma.sync with x in fp16 hi/lo parts, scale per sub-block) is sb_flow_core.cuh,
+// a variant of sb_iq3s_core.cuh's with an 8-byte table of fp16 pairs.
 //
 // Every wait is bounded (stage barriers, sequence stamps, pair polls). A CTA
 // that gives up records SB_DERR_TIMEOUT, raises a global abort word that the

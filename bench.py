@@ -182,6 +182,25 @@ def build_cfg2_bank(dev, stream, rank: int = 0, layers: int = LAYERS):
     return bank, views
 
 
+def chain_f64(x_rows, layer_banks, ids_lt, w_lt, qts, d_model, ff):
+    """fp64 chain of reference_block for the tokens of x_rows [T][d_model] over
+    the given layers: layer_banks[L] = (gate, up, down) device tensors of
+    [n_experts][expert bytes] rows, ids_lt / w_lt [L][T][K]. A layer's distinct
+    experts are copied to the host once for all tokens (the oracle, test
+    infrastructure; outside any timing)."""
+    from oracle import cpu as orc
+    want = np.asarray(x_rows, np.float64).copy()
+    for Lr, (g, u, d) in enumerate(layer_banks):
+        sel = np.unique(ids_lt[Lr])
+        pos = {int(e): i for i, e in enumerate(sel)}
+        gs, us, ds = (np.stack([t[int(e)].cpu().numpy() for e in sel]) for t in (g, u, d))
+        for t in range(want.shape[0]):
+            slots = np.array([pos[int(e)] for e in ids_lt[Lr][t]], np.int32)
+            want[t] = want[t] + orc.moe_block_f64(gs, us, ds, slots, w_lt[Lr][t], want[t].astype(np.float32),
+                                                  d_model, ff, *qts)
+    return want
+
+
 def cfg2_parity(views, ids_set, w_set, x_first) -> float:
     """Decode one token of the benchmark (routing ids_set / w_set [layers][1][K],
     input x_first [1][d_model]) once through sabah_moe_decode, eagerly, and
@@ -559,6 +578,24 @@ def run_ep(args, rank: int, world: int, local_rank: int):
         if world > 1:
             dist.barrier()
 
+    # parity of the timed shape at N = 1 (one rank holds every expert): routing
+    # set 0, all blocks, the first two sequences, against the fp64 chain
+    # (before timing; fails loudly). At N > 1 no rank holds the whole bank;
+    # tests/test_gpu_ep.py checks 2 ranks against the single-GPU decode.
+    parity = None
+    if not args.no_parity and world == 1:
+        from oracle import cpu as orc
+        with torch.cuda.stream(stream):
+            step(0)
+        stream.synchronize()
+        lb = [tuple(t.view(n_loc, -1) for t in b) for b in banks]
+        want = chain_f64(x_all0[:2], lb, ids_np[0][:, :2], w_np[0][:, :2], (QT_IQ3_S, QT_IQ3_S, QT_IQ3_S),
+                         D_MODEL, FF)
+        got = x.cpu().numpy()[:2]
+        parity = max(float(orc.rel_l2(got[t], want[t])) for t in range(2))
+        if not parity <= 2e-3:
+            raise SystemExit("cfg5 parity failed: rel-L2 %.3e against the fp64 chain" % parity)
+
     # warm every routing set (the runtime sizes its scratch), then one CUDA graph
     # per set: the 48 blocks' kernels and NCCL collectives replay without host work
     with torch.cuda.stream(stream):
@@ -681,6 +718,9 @@ def run_ep(args, rank: int, world: int, local_rank: int):
                 "path": "ep.decode_step (C ABI kernels + NCCL), host plans per step in one packed upload"},
         "gpu_launches": int(launches_per_step * args.steps),
         "clocks": clk,
+        "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3,
+                   "checked": "N = 1: routing set 0, all %d blocks, sequences 0-1 (worst), before timing" % LAYERS}
+        if parity is not None else None,
     }
 
 
@@ -737,6 +777,33 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
         ops.mul_mat_id(up, GU_EXPERT, GU_ROW, x, ids_d[s], FF, D_MODEL, EXPERTS, QT_IQ3_S, out=u_out, stream=stream)
         ops.mul_mat_id(down, D_EXPERT, D_ROW, h, ids_d[s], D_MODEL, FF, EXPERTS, QT_IQ3_S, out=d_out, stream=stream)
 
+    # parity of the timed shape: routing set 0, 8 sampled tokens, all three calls
+    # (every slot) against the fp64 oracle (before timing; fails loudly)
+    parity = None
+    if not args.no_parity:
+        from oracle import cpu as orc
+        with torch.cuda.stream(stream):
+            step(0)
+        stream.synchronize()
+        sample = np.random.default_rng(24).choice(T, 8, replace=False)
+        ids_s = ids_np[0][sample]
+        xs, hs = x.cpu().numpy()[sample], h.cpu().numpy()[sample]
+        worst = 0.0
+        for bank_t, rows, kk, xin, got_t, per in ((gate, FF, D_MODEL, xs, g_out, GU_EXPERT),
+                                                  (up, FF, D_MODEL, xs, u_out, GU_EXPERT),
+                                                  (down, D_MODEL, FF, hs, d_out, D_EXPERT)):
+            sel = np.unique(ids_s)
+            pos = np.searchsorted(sel, ids_s).astype(np.int32)
+            sub = np.stack([bank_t[int(e) * per:(int(e) + 1) * per].cpu().numpy() for e in sel]).reshape(-1)
+            rb = per // rows
+            want = orc.mmid_f64(sub, per, rb, xin, xin.shape[1], pos, rows, kk, len(sel), QT_IQ3_S)
+            got = got_t.cpu().numpy()[sample].astype(np.float64)
+            worst = max(worst, max(float(np.linalg.norm(got[t, i] - want[t, i]) / np.linalg.norm(want[t, i]))
+                                   for t in range(len(sample)) for i in range(K)))
+        parity = worst
+        if not parity <= 2e-3:
+            raise SystemExit("cfg3 parity failed: rel-L2 %.3e against fp64" % parity)
+
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             step(i % PF_SETS)
@@ -785,6 +852,9 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
                                  for k, v in ktimes.items()}},
         "gpu_launches": int(sum(v[0] for v in ktimes.values()) * args.steps),
         "clocks": clk,
+        "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3,
+                   "checked": "routing set 0, 8 sampled tokens x 10 slots of the gate, up and down calls (worst), "
+                              "before timing"} if parity is not None else None,
     }
 
 
@@ -1277,6 +1347,26 @@ def run_mixed(args, rank: int, world: int, local_rank: int):
         x_d.copy_(x0_d)
         decode(ids_d[s].data_ptr(), w_d[s].data_ptr(), stream)
 
+    # parity of the timed shape: routing set 0, all blocks, every token, against
+    # the fp64 chain (before timing; fails loudly)
+    parity = None
+    if not args.no_parity:
+        with torch.cuda.stream(stream):
+            step(0)
+        stream.synchronize()
+        banks = []
+        for Lr in range(LAYERS):
+            base = Lr * layer_bytes
+            gv = bank[base: base + EXPERTS * MX_GU_EXPERT].view(EXPERTS, MX_GU_EXPERT)
+            uv = bank[base + EXPERTS * MX_GU_EXPERT: base + 2 * EXPERTS * MX_GU_EXPERT].view(EXPERTS, MX_GU_EXPERT)
+            dv = bank[base + 2 * EXPERTS * MX_GU_EXPERT: base + layer_bytes].view(EXPERTS, MX_D_EXPERT)
+            banks.append((gv, uv, dv))
+        from oracle import cpu as orc
+        want = chain_f64(x0_np, banks, ids_np[0], w_np[0], (QT_Q4_K, QT_Q4_K, QT_Q6_K), D_MODEL, FF)
+        got = x_d.cpu().numpy()
+        parity = max(float(orc.rel_l2(got[t], want[t])) for t in range(T))
+        if not parity <= 2e-3:
+            raise SystemExit("cfg4 parity failed: rel-L2 %.3e against the fp64 chain" % parity)
     # one graph per routing set (x <- x0, then the 48 blocks), captured after a
     # warm-up pass has sized the runtime's scratch
     with torch.cuda.stream(stream):
@@ -1383,6 +1473,9 @@ def run_mixed(args, rank: int, world: int, local_rank: int):
                 "path": "sabah_moe_decode (C ABI), eager launches"},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clk,
+        "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3,
+                   "checked": "routing set 0, all %d blocks, every token (worst), before timing" % LAYERS}
+        if parity is not None else None,
     }
 
 

@@ -102,6 +102,10 @@ struct SmallParams {
     float* h;                      // [T][n_used][ff]
     float* v;                      // [T][n_used][d_model] unweighted down rows
     int* err;
+    // the down kernel of a block call: the call's gate/up kernel releases its
+    // dependents only once its own grid dependency (the router ids' writer) is
+    // done, so this kernel may read the ids before its own wait
+    int ids_ready;
 };
 
 __device__ inline void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
@@ -428,19 +432,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_small(const __grid_constant__ S
     // programmatic dependent launch: the next kernel on the stream may start its
     // prologue (barrier set-up) as SMs free up. Everything this kernel reads
     // that an earlier kernel may write (router ids, x, h, v), and every global
-    // write, comes after griddepcontrol.wait.
-    asm volatile("griddepcontrol.launch_dependents;");
-    if (warp == kW) {
-        // the plan reads the router ids, which the previous kernel on the
-        // stream may have written: wait for it first
+    // write, comes after griddepcontrol.wait. The gate/up kernel releases its
+    // dependents only after that wait, so the block's down kernel (ids_ready)
+    // builds its routing plan from final ids while gate/up still runs.
+    if (!GU && p.ids_ready) {
+        asm volatile("griddepcontrol.launch_dependents;");
+        if (warp == kW) {
+            build_plan(p, smem);
+            plan_arrive();
+        }
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        build_plan(p, smem);
-        plan_arrive();
+        if (warp != kW) plan_wait();
     } else {
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        if (GU)   // the tokens' x, rows 0..T-1
-            stage_rows(smem, kMaxTok, p.k, [&](int r) { return r < p.n_tokens ? p.x + (size_t)r * p.d_model : nullptr; });
-        plan_wait();
+        asm volatile("griddepcontrol.launch_dependents;");
+        if (warp == kW) {
+            build_plan(p, smem);
+            plan_arrive();
+        } else {
+            if (GU)   // the tokens' x, rows 0..T-1
+                stage_rows(smem, kMaxTok, p.k,
+                           [&](int r) { return r < p.n_tokens ? p.x + (size_t)r * p.d_model : nullptr; });
+            plan_wait();
+        }
     }
 
     const int nd = ((const int*)(smem + Smem::misc))[0];
@@ -778,6 +792,7 @@ int sb_try_block_small(const sb_block_args& a, cudaStream_t st) {
     if (!ok1) return -1;
     const int t2 = sb_timing_begin("small_kq_down", st);
     SmallParams pd = p;
+    pd.ids_ready = 1;   // launched right after this call's gate/up kernel
     pd.rb = rb_dn;
     pd.rs = rs_dn;
     pd.k = a.ff;

@@ -122,6 +122,10 @@ struct Params {
     float* partial;        // DOWN: [T][n_used][d_model]; GATE_UP: [T][n_used][2][ff]
     int* counters;         // DOWN: [T][d_model / 16]; GATE_UP: [T][n_used][ff / 16]; self-resetting
     int* err;
+    // the down launch of a block call: the call's gate/up launch releases its
+    // dependents only after its own grid dependency (the ids' writer) is done,
+    // so this launch may read the ids and stream its tiles before its own wait
+    int ids_ready;
 };
 
 __device__ inline void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory"); }
@@ -180,8 +184,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
     volatile int* abort_flag = (volatile int*)(smem + Smem::abort_flag);
     Desc* descs = (Desc*)(smem + Smem::desc);
 
-    // let the next kernel on the stream begin its prologue as SMs free up
-    asm volatile("griddepcontrol.launch_dependents;");
+    // let the next kernel on the stream begin its prologue as SMs free up: at
+    // once when this launch's ids are known to be final, else after its grid
+    // dependency (below), so that the next launch may trust the ids
+    if (p.ids_ready) asm volatile("griddepcontrol.launch_dependents;");
 
     // this CTA's item range
     const int i0 = (int)((long long)blockIdx.x * p.n_items / gridDim.x);
@@ -205,7 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
         // may have written (a router that triggers its dependents early), so
         // the producer reads them only after that kernel has completed. The
         // barrier set-up above and the consumers' table fill still overlap it.
-        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (!p.ids_ready) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            asm volatile("griddepcontrol.launch_dependents;");
+        }
         // lane l issues sequence numbers n = l, l + kIssuers, ... (stage n % ns,
         // always the same lane for a given stage); each lane looks up its own
         // tiles' expert addresses, so those loads overlap across lanes
@@ -249,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_iq3s(const Params p) {
     if constexpr (QT == SB_IQ3_S) fill_table<kConsumers * 32>(table);
     // activations and outputs only after the previous kernel on the stream is done
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (!p.ids_ready) asm volatile("griddepcontrol.launch_dependents;");
 
     const int g = lane >> 2, c = lane & 3;
     const uint32_t boff = lane_boff(lane);
@@ -688,8 +698,10 @@ int block_two_launches(const sb_block_args& a, int qt, cudaStream_t st) {
     p.partial = g_bs.gu_partial;
     p.counters = g_bs.gu_counters;
     if (launch(p, qt, st) < 0) return -1;
-    // down + weighted combine: items (t, e, row tile)
+    // down + weighted combine: items (t, e, row tile); launched right after the
+    // gate/up launch, which released its dependents only once the ids were final
     p.mode = MODE_DOWN;
+    p.ids_ready = 1;
     p.rtiles = a.d_model / 16;
     p.n_items = a.n_tokens * a.n_used * p.rtiles;
     p.per_key = p.rtiles;               // one h per (token, slot)
@@ -767,6 +779,7 @@ int sb_block_iq3s_fixed(const sb_block_args& a, cudaStream_t st) {
     p.counters = (int*)fs.ptr;
     if (launch<SB_IQ3_S>(p, st) < 0) return -1;
     p.mode = MODE_DOWN;
+    p.ids_ready = 1;   // right after the gate/up launch (see block_two_launches)
     p.rtiles = a.d_model / 16;
     p.n_items = a.n_tokens * a.n_used * p.rtiles;
     p.per_key = p.rtiles;

@@ -557,8 +557,10 @@ struct DecodeScratch {
     bool stale = false;
 };
 DecodeScratch g_ds;
-bool g_attr_set = false;
-int g_grid = 0;
+// launch attribute and grid, per device (the smem opt-in is a per-device setting)
+constexpr int kMaxDev = 64;
+bool g_attr_set[kMaxDev] = {};
+int g_grid[kMaxDev] = {};
 
 bool fast_path_enabled() {
     static int on = -1;
@@ -607,20 +609,23 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
     p.dn.per_key = p.dn.rowpair ? p.dn.rtiles / 2 : p.dn.rtiles * pairs;   // items of one token
     p.dn.per_unit = p.dn.rowpair ? 1 : pairs;    // 32 rows of one slot, or 16 rows over all slots
 
-    if (!g_attr_set) {
+    int dev = 0;
+    if (!sb_cuda_ok(cudaGetDevice(&dev), "decode device")) return -1;
+    if (dev < 0 || dev >= kMaxDev) return 0;
+    if (!g_attr_set[dev]) {
         if (!sb_cuda_ok(cudaFuncSetAttribute(k_decode_iq3s, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::total),
                         "decode smem attribute"))
             return -1;
-        int dev = 0, sms = 0, per_sm = 0;
-        cudaGetDevice(&dev);
+        int sms = 0, per_sm = 0;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (!sb_cuda_ok(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_iq3s, kThreads, Smem::total),
                         "decode occupancy"))
             return -1;
-        g_grid = sms * std::max(per_sm, 0);
-        g_attr_set = true;
+        g_grid[dev] = sms * std::max(per_sm, 0);
+        g_attr_set[dev] = true;
     }
-    if (g_grid < 1) return 0;
+    const int grid = g_grid[dev];
+    if (grid < 1) return 0;
 
     // scratch: the barrier words (zeroed, self-resetting), then the down-phase sets of h
     const size_t sync_b = 256;
@@ -671,7 +676,7 @@ int sb_try_decode_iq3s(const sb_decode_args& a, cudaStream_t st) {
 
     const int tslot = sb_timing_begin("decode_iq3s", st);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(g_grid);
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Smem::total;
     cfg.stream = st;

@@ -644,16 +644,21 @@ __global__ void k_x_split(const uint8_t* x, size_t x_id_stride, size_t x_token_s
 // ------------------------------------------------------------ register-decode grouped kernel
 // For experts with at most 8 routed pairs. A CTA task is (expert, 128-row
 // block): the producer warp bulk-copies the pairs' x rows (fp16 hi and lo
-// parts, split once per x row) and one 16-row weight tile per consumer warp
-// into shared memory; each of the 8 consumer warps then walks the IQ3_S
-// sub-blocks of its tile, decodes its A fragments once (mma.sync m16n8k16;
+// parts, split once per x row) and eight 16-row weight tiles into shared
+// memory, its lanes issuing the copies side by side. Two consumer warps share
+// a tile, one per half of its super-blocks (16 warps: enough independent work
+// per SM to hide the latency of the shared loads and lookups). Each walks the
+// IQ3_S sub-blocks of its half, decodes its A fragments once (mma.sync m16n8k16;
 // the MMA's k slots {2c, 2c+1, 2c+8, 2c+9} are mapped to the 4 weights of grid
 // entry c, placed as fp16 subnormals b * 2^-24 with their signs) and multiplies
 // them with the pairs' x (the 8 pairs are the MMA's 8 columns); the sub-block's
-// scale is applied to the fp32 partial sums. x and weights come from shared
-// memory, so the K loop never waits on L2.
-constexpr int kGW = 8;                       // consumer warps (16 rows each: one 128-row block)
-constexpr int kGThreads = (kGW + 1) * 32;    // + the producer warp
+// scale is applied to the fp32 partial sums. The second half's warp hands
+// its sums to the first half's through shared memory (an mbarrier per tile),
+// which adds them in that order and writes the rows. x and weights come from
+// shared memory, so the K loop never waits on L2.
+constexpr int kGW = 8;                       // 16-row tiles per task (one 128-row block)
+constexpr int kGC = 2 * kGW;                 // consumer warps: (tile, half of the super-blocks)
+constexpr int kGThreads = (kGC + 1) * 32;    // + the producer warp
 constexpr int kGTile = 16 * 880;             // a 16-row tile at k <= 2048
 constexpr int kGRep = 16;                    // grid-table replicas (lane % 16: at most 2-way bank conflicts)
 constexpr int kGXRow = 2048 * 2 + 32;        // bytes per staged x row (fp16, padded against bank conflicts)
@@ -663,8 +668,9 @@ struct MmaSmem {
     static constexpr int xh = grid + 512 * kGRep * 4;                // [kGMaxPairs][kGXRow]
     static constexpr int xl = xh + kGMaxPairs * kGXRow;              // [kGMaxPairs][kGXRow]
     static constexpr int tiles = xl + kGMaxPairs * kGXRow;           // [kGW][kGTile]
-    static constexpr int bars = tiles + kGW * kGTile;                // xbar, free, tile[kGW]
-    static constexpr int total = bars + (2 + kGW) * 8;
+    static constexpr int part = tiles + kGW * kGTile;                // [kGW][32 lanes][4] float: second-half sums
+    static constexpr int bars = part + kGW * 32 * 16;                // xbar, free, tile[kGW], part[kGW]
+    static constexpr int total = bars + (2 + 2 * kGW) * 8;
 };
 static_assert(MmaSmem::total <= 227 * 1024, "shared memory budget");
 static_assert(MmaSmem::xh % 16 == 0 && MmaSmem::xl % 16 == 0 && MmaSmem::tiles % 16 == 0 && kGXRow % 16 == 0 &&
@@ -703,6 +709,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint32_t* gtab = (uint32_t*)(smem + MmaSmem::grid);
     const uint32_t xbar = smem_u32(smem + MmaSmem::bars), freebar = xbar + 8, tbar0 = xbar + 16;
+    const uint32_t pbar0 = tbar0 + 8 * kGW;   // per tile: the second half's sums are in
     volatile int* abort_flag = nullptr;
     __shared__ int s_abort;
     for (int e = threadIdx.x; e < 512; e += kGThreads) {
@@ -713,8 +720,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
     if (threadIdx.x == 0) {
         s_abort = 0;
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(xbar));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(freebar), "r"(kGW));
-        for (int w = 0; w < kGW; ++w) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tbar0 + 8 * w));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(freebar), "r"(kGC));
+        for (int w = 0; w < 2 * kGW; ++w) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tbar0 + 8 * w));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -727,48 +734,53 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
         return t;
     };
 
-    if (warp == kGW) {
-        // ---------------------------------------------------------- producer (lane 0)
-        if (lane == 0) {
-            int i = 0, last = -1;
-            for (int ti = blockIdx.x; ti < n_tasks; ti += gridDim.x, ++i) {
-                // the consumers are done with the previous task's buffers
-                if (i > 0 && !mbar_wait(freebar, (i - 1) & 1, p.err, abort_flag)) break;
-                const Task t = task_at(ti);
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == kGC) {
+        // ---------------------------------------------------------- producer
+        // lane 0 sets the x barrier's byte count; then lanes j < n copy pair j's
+        // hi part, lanes 8 + j its lo part, lanes 16 + w tile w
+        int i = 0, last = -1;
+        for (int ti = blockIdx.x; ti < n_tasks; ti += gridDim.x, ++i) {
+            // the consumers are done with the previous task's buffers
+            if (!__all_sync(0xffffffffu, i == 0 || mbar_wait(freebar, (i - 1) & 1, p.err, abort_flag))) break;
+            const Task t = task_at(ti);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            if (lane == 0)
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
                              "r"(2u * xrow_bytes * (uint32_t)t.n)
                              : "memory");
-                for (int j = 0; j < t.n; ++j) {
-                    const int xr = p.pairs[t.n0 + j].xrow;
-                    bulk_copy(smem_u32(smem + MmaSmem::xh + j * kGXRow), p.xh + (size_t)xr * p.k, xrow_bytes, xbar);
-                    bulk_copy(smem_u32(smem + MmaSmem::xl + j * kGXRow), p.xl + (size_t)xr * p.k, xrow_bytes, xbar);
-                }
+            __syncwarp();
+            if (lane < 16 && (lane & 7) < t.n) {
+                const int j = lane & 7;
+                const int xr = p.pairs[t.n0 + j].xrow;
+                const size_t o = (size_t)xr * p.k;
+                if (lane < 8)
+                    bulk_copy(smem_u32(smem + MmaSmem::xh + j * kGXRow), p.xh + o, xrow_bytes, xbar);
+                else
+                    bulk_copy(smem_u32(smem + MmaSmem::xl + j * kGXRow), p.xl + o, xrow_bytes, xbar);
+            } else if (lane >= 16 && lane < 16 + kGW) {
+                const int w = lane - 16;
                 const uint8_t* blk = p.base + (size_t)t.expert * p.expert_stride + (size_t)t.mt * kGW * tile_bytes;
-                for (int w = 0; w < kGW; ++w) {
-                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tbar0 + 8 * w),
-                                 "r"(tile_bytes)
-                                 : "memory");
-                    bulk_copy(smem_u32(smem + MmaSmem::tiles + w * kGTile), blk + (size_t)w * tile_bytes, tile_bytes,
-                              tbar0 + 8 * w);
-                }
-                if (ti + (int)gridDim.x < n_tasks) {   // the next task's weights, into L2 meanwhile
-                    const Task tn = task_at(ti + gridDim.x);
-                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
-                                     p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * kGW * tile_bytes),
-                                 "r"(kGW * tile_bytes)
-                                 : "memory");
-                }
-                last = i;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tbar0 + 8 * w),
+                             "r"(tile_bytes)
+                             : "memory");
+                bulk_copy(smem_u32(smem + MmaSmem::tiles + w * kGTile), blk + (size_t)w * tile_bytes, tile_bytes,
+                          tbar0 + 8 * w);
+            } else if (lane == 31 && ti + (int)gridDim.x < n_tasks) {   // the next task's weights, into L2 meanwhile
+                const Task tn = task_at(ti + gridDim.x);
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                                 p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * kGW * tile_bytes),
+                             "r"(kGW * tile_bytes)
+                             : "memory");
             }
-            // never leave with copies in flight: the last task's copies have landed
-            if (last >= 0) {
-                for (long long it = 0; it < kSpinLimit && !mbar_try_wait(xbar, last & 1); ++it) {
-                }
-                for (int w = 0; w < kGW; ++w)
-                    for (long long it = 0; it < kSpinLimit && !mbar_try_wait(tbar0 + 8 * w, last & 1); ++it) {
-                    }
+            last = i;
+        }
+        // never leave with copies in flight: the last task's copies have landed
+        if (last >= 0 && lane == 0) {
+            for (long long it = 0; it < kSpinLimit && !mbar_try_wait(xbar, last & 1); ++it) {
             }
+            for (int w = 0; w < kGW; ++w)
+                for (long long it = 0; it < kSpinLimit && !mbar_try_wait(tbar0 + 8 * w, last & 1); ++it) {
+                }
         }
         return;
     }
@@ -776,21 +788,26 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
     // -------------------------------------------------------------- consumers
     const int g = lane >> 2, c = lane & 3;
     const uint32_t grep = (uint32_t)(lane & (kGRep - 1));
-    const uint8_t* tile = smem + MmaSmem::tiles + warp * kGTile;
+    const int tw = warp & (kGW - 1), kh = warp / kGW;   // tile, half of the super-blocks
+    const uint8_t* tile = smem + MmaSmem::tiles + tw * kGTile;
+    float4* part = (float4*)(smem + MmaSmem::part) + tw * 32 + lane;
+    const int nsb = p.k / 256, sb_mid = (nsb + 1) / 2;
+    const int j_lo = kh ? sb_mid : 0, j_hi = kh ? nsb : sb_mid;
     const uint8_t* xhs = smem + MmaSmem::xh + g * kGXRow;   // this lane's pair column g
     const uint8_t* xls = smem + MmaSmem::xl + g * kGXRow;
     int i = 0;
     for (int ti = blockIdx.x; ti < n_tasks; ti += gridDim.x, ++i) {
         const Task t = task_at(ti);
-        const bool ok = mbar_wait(xbar, i & 1, p.err, abort_flag) && mbar_wait(tbar0 + 8 * warp, i & 1, p.err, abort_flag);
+        const bool ok = mbar_wait(xbar, i & 1, p.err, abort_flag) && mbar_wait(tbar0 + 8 * tw, i & 1, p.err, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) break;
         const bool have = g < t.n;   // pair column g exists (else its B is zero)
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         // super-block by super-block: its scale d and 4 scale bytes are read
         // once, and its 8 sub-blocks are unrolled so their loads, lookups and
-        // MMAs overlap (the kernel runs 9 warps per SM, so a warp needs
-        // independent work of its own to hide latency)
-        for (int j = 0; j < p.k / 256; ++j) {
+        // MMAs overlap (a warp needs independent work of its own to hide
+        // latency: unrolling 4 sub-blocks instead, with the halves split by
+        // sub-block, measured 7% slower on the whole prefill step)
+        for (int j = j_lo; j < j_hi; ++j) {
             float d[2];
             uint32_t scw[2];
 #pragma unroll
@@ -840,8 +857,24 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
                 acc[3] = fmaf(db[1], dd[3], acc[3]);
             }
         }
+        if (kh == 1) {
+            // hand the second half's sums to the tile's first-half warp
+            *part = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pbar0 + 8 * tw) : "memory");
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(freebar) : "memory");
+            continue;
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(pbar0 + 8 * tw, i & 1, p.err, abort_flag))) break;
+        {
+            const float4 q = *part;
+            acc[0] += q.x;
+            acc[1] += q.y;
+            acc[2] += q.z;
+            acc[3] += q.w;
+        }
         // D: (row g, pair 2c), (row g, pair 2c + 1), (row g + 8, pair 2c), (row g + 8, pair 2c + 1)
-        const int row0 = (t.mt * kGW + warp) * 16;
+        const int row0 = (t.mt * kGW + tw) * 16;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const int n = 2 * c + u;

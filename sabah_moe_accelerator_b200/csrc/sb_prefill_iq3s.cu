@@ -212,6 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_prefill_iq3s(const GemmParams p
     int* pair_exp = (int*)(smem + Smem::pair_exp);
     float** pair_dst = (float**)(smem + Smem::pair_dst);
     uint32_t* gtab = (uint32_t*)(smem + Smem::grid);
+    // the register-decode kernel launched after this one reads nothing this
+    // kernel writes: its CTAs may take the SMs this kernel's CTAs leave
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (tid == 0) {
         *abort_flag = 0;
@@ -500,6 +503,7 @@ struct GroupParams {
                       // most kGMaxPairs): {expert, -, first pair, pairs}; a task is (entry,
                       // 128-row block), task index = entry * m_tiles + block
     int* n_mtasks;    // entries * m_tiles
+    int* mnext;       // the register-decode kernel's next task (zeroed by the plan)
     int heavy;
     int* order;       // [pairs] pair index in grouped order
     PairInfo* pairs;  // [pairs] grouped order
@@ -569,6 +573,7 @@ __global__ void k_group_plan(const GroupParams g) {
     if (threadIdx.x == 1023) {
         *g.n_tasks = s_tsum[1023];
         *g.n_mtasks = s_msum[1023] * g.m_tiles;
+        *g.mnext = 0;
     }
 }
 
@@ -683,6 +688,7 @@ struct MmaParams {
     int rb, k, m_tiles;
     const Task* tasks;            // {expert, -, first pair, pairs}
     const int* n_tasks;           // entries * m_tiles
+    int* next;                    // tasks are taken in order from this counter
     const PairInfo* pairs;
     const __half* xh;
     const __half* xl;
@@ -712,6 +718,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
     const uint32_t pbar0 = tbar0 + 8 * kGW;   // per tile: the second half's sums are in
     volatile int* abort_flag = nullptr;
     __shared__ int s_abort;
+    __shared__ int s_task;   // the current task (-1: none left), read after the x barrier
     for (int e = threadIdx.x; e < 512; e += kGThreads) {
         const uint32_t w = sb_iq3s_grid[e];
 #pragma unroll
@@ -736,18 +743,35 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
 
     if (warp == kGC) {
         // ---------------------------------------------------------- producer
-        // lane 0 sets the x barrier's byte count; then lanes j < n copy pair j's
-        // hi part, lanes 8 + j its lo part, lanes 16 + w tile w
+        // Tasks come in order from a global counter, so CTAs that start late
+        // (on SMs the tcgen05 kernel still held) take fewer. Lane 0 takes a task,
+        // publishes it and sets the x barrier's byte count; then lanes j < n copy
+        // pair j's hi part, lanes 8 + j its lo part, lanes 16 + w tile w. With no
+        // task left, lane 0 publishes -1 and arrives on the x barrier alone.
         int i = 0, last = -1;
-        for (int ti = blockIdx.x; ti < n_tasks; ti += gridDim.x, ++i) {
+        bool drained = false;
+        for (;; ++i) {
             // the consumers are done with the previous task's buffers
             if (!__all_sync(0xffffffffu, i == 0 || mbar_wait(freebar, (i - 1) & 1, p.err, abort_flag))) break;
+            int ti = 0;
+            if (lane == 0) ti = atomicAdd(p.next, 1);
+            ti = __shfl_sync(0xffffffffu, ti, 0);
+            if (ti >= n_tasks) {
+                if (lane == 0) {
+                    s_task = -1;
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(xbar) : "memory");
+                }
+                drained = true;   // every copy issued so far was consumed
+                break;
+            }
             const Task t = task_at(ti);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            if (lane == 0)
+            if (lane == 0) {
+                s_task = ti;
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(xbar),
                              "r"(2u * xrow_bytes * (uint32_t)t.n)
                              : "memory");
+            }
             __syncwarp();
             if (lane < 16 && (lane & 7) < t.n) {
                 const int j = lane & 7;
@@ -765,7 +789,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
                              : "memory");
                 bulk_copy(smem_u32(smem + MmaSmem::tiles + w * kGTile), blk + (size_t)w * tile_bytes, tile_bytes,
                           tbar0 + 8 * w);
-            } else if (lane == 31 && ti + (int)gridDim.x < n_tasks) {   // the next task's weights, into L2 meanwhile
+            } else if (lane == 31 && ti + (int)gridDim.x < n_tasks) {   // a task about one round on, into L2
                 const Task tn = task_at(ti + gridDim.x);
                 asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
                                  p.base + (size_t)tn.expert * p.expert_stride + (size_t)tn.mt * kGW * tile_bytes),
@@ -774,14 +798,16 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
             }
             last = i;
         }
-        // never leave with copies in flight: the last task's copies have landed
-        if (last >= 0 && lane == 0) {
+        // never leave with copies in flight: after a give-up, the last task's copies have landed
+        if (!drained && last >= 0 && lane == 0) {
             for (long long it = 0; it < kSpinLimit && !mbar_try_wait(xbar, last & 1); ++it) {
             }
             for (int w = 0; w < kGW; ++w)
                 for (long long it = 0; it < kSpinLimit && !mbar_try_wait(tbar0 + 8 * w, last & 1); ++it) {
                 }
         }
+        // this kernel's stream successors also wait for the tcgen05 kernel's rows
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         return;
     }
 
@@ -795,11 +821,12 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
     const int j_lo = kh ? sb_mid : 0, j_hi = kh ? nsb : sb_mid;
     const uint8_t* xhs = smem + MmaSmem::xh + g * kGXRow;   // this lane's pair column g
     const uint8_t* xls = smem + MmaSmem::xl + g * kGXRow;
-    int i = 0;
-    for (int ti = blockIdx.x; ti < n_tasks; ti += gridDim.x, ++i) {
+    for (int i = 0;; ++i) {
+        if (!__all_sync(0xffffffffu, mbar_wait(xbar, i & 1, p.err, abort_flag))) break;
+        const int ti = *(volatile int*)&s_task;
+        if (ti < 0) break;
         const Task t = task_at(ti);
-        const bool ok = mbar_wait(xbar, i & 1, p.err, abort_flag) && mbar_wait(tbar0 + 8 * tw, i & 1, p.err, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(tbar0 + 8 * tw, i & 1, p.err, abort_flag))) break;
         const bool have = g < t.n;   // pair column g exists (else its B is zero)
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         // super-block by super-block: its scale d and 4 scale bytes are read
@@ -888,6 +915,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_group_mma_iq3s(const MmaParams
         __syncwarp();   // every lane is done with the buffers
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(freebar) : "memory");
     }
+    // this kernel's stream successors also wait for the tcgen05 kernel's rows
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // ------------------------------------------------------------ host side
@@ -985,6 +1014,7 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
     uint8_t* q = b + b_counts + b_cursor + b_tasks;
     g.n_tasks = (int*)q;
     g.n_mtasks = (int*)(q + 16);
+    g.mnext = (int*)(q + 32);
     q += b_ntasks;
     g.mtasks = (Task*)q;
     q += b_mtasks;
@@ -1042,13 +1072,27 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
     mp.m_tiles = m_tiles;
     mp.tasks = g.mtasks;
     mp.n_tasks = g.n_mtasks;
+    mp.next = g.mnext;
     mp.pairs = g.pairs;
     mp.xh = xh;
     mp.xl = xl;
     mp.xexp = xexp;
     mp.dst = (uint8_t*)a.dst;
     mp.err = a.err;
-    k_group_mma_iq3s<<<g_grid, kGThreads, MmaSmem::total, st>>>(mp);   // the rest
+    {   // the rest: a programmatic dependent of the tcgen05 kernel, whose SMs it
+        // takes as that kernel's CTAs finish
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(g_grid);
+        cfg.blockDim = dim3(kGThreads);
+        cfg.dynamicSmemBytes = MmaSmem::total;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (!sb_cuda_ok(cudaLaunchKernelEx(&cfg, k_group_mma_iq3s, mp), "grouped mma launch")) return -1;
+    }
     sb_timing_end(tslot, st);
     return sb_cuda_ok(cudaGetLastError(), "prefill launch") ? 1 : -1;
 }

@@ -925,6 +925,7 @@ def run_stream(args, rank: int, world: int, local_rank: int):
     import torch
     os.environ.setdefault("SABAH_LLAMA_HOT_BYTES", str(int(ST_SLAB)))
     os.environ["SABAH_LLAMA_LAYER_MERGE"] = "1" if args.layer_merge == "on" else "0"
+    os.environ["SABAH_LLAMA_PREFETCH"] = "1" if args.prefetch == "on" else "0"
     from sabah_moe_accelerator_b200 import ops, rt
 
     dev = torch.device("cuda", local_rank)
@@ -1052,7 +1053,9 @@ def run_stream(args, rank: int, world: int, local_rank: int):
     hits = (s1["hits"] - s0["hits"]) / args.steps
     fill_gbs = fetched / (ms * 1e-3) / 1e9
     fill_io = {k: s1[k] - s0[k] for k in ("staged_bytes", "pinned_fill_bytes", "direct_io_reads", "direct_io_bytes",
-                                          "direct_io_fallbacks", "fill_waves", "merged_slots")}
+                                          "direct_io_fallbacks", "fill_waves", "merged_slots", "prefetch_reads",
+                                          "prefetch_used", "prefetch_stale", "prefetch_dropped", "prefetch_waits",
+                                          "prefetch_wait_timeouts")}
     del host, views
     if from_file:
         del bank
@@ -1068,7 +1071,7 @@ def run_stream(args, rank: int, world: int, local_rank: int):
                 % ("a bank file" if from_file else "pinned host memory"),
         "config": {"workload": ST_WORKLOAD if from_file else ST_WORKLOAD_PINNED, "layers": ST_LAYERS, "experts": EXPERTS, "hidden": D_MODEL, "ffn": FF,
                    "top_k": TOP_K, "slab_bytes": int(float(os.environ["SABAH_LLAMA_HOT_BYTES"])),
-                   "layer_merge": args.layer_merge,
+                   "layer_merge": args.layer_merge, "prefetch": args.prefetch,
                    "host_bank_bytes": ST_LAYERS * layer_bytes, "tokens_per_step": 1,
                    "l2": "bank 16.6 GB in host memory, slab 9.8 GB, both far above L2"},
         "roofline": {"bound": "pcie", "achieved": round(fill_gbs, 2), "peak": round(h2d_gbs, 1), "unit": "GB/s",
@@ -1496,6 +1499,9 @@ def main():
                          "host-resident bank streamed through the hot-tier slab")
     ap.add_argument("--exchange", default="ag", choices=["ag", "a2a"],
                     help="cfg5: the expert-parallel exchange (all-gather + reduce-scatter, or all-to-all)")
+    ap.add_argument("--prefetch", default="off", choices=["on", "off"],
+                    help="cfg5s: the staging readahead (SABAH_LLAMA_PREFETCH): the first call of a layer has the "
+                         "followers' missing experts read into pinned buffers; it runs only with --layer-merge off")
     ap.add_argument("--layer-merge", default="on", choices=["on", "off"],
                     help="cfg5s: the merged layer fetch (SABAH_LLAMA_LAYER_MERGE): a layer's three tensors' misses "
                          "in one read wave")

@@ -287,6 +287,9 @@ struct Chain {
     uint64_t merged_slots = 0;   // follower slots filled in an earlier call's wave
 } g_chain;
 
+// the readahead pays only when a call has few ids (ref SB_PF_MAX_TOKENS)
+constexpr int kPfMaxTokens = 4;
+
 bool layer_merge_enabled() {
     const char* v = std::getenv("SABAH_LLAMA_LAYER_MERGE");
     return v && (!std::strcmp(v, "1") || !std::strcmp(v, "on"));
@@ -425,11 +428,14 @@ bool fill_locked(const std::vector<Fetch>& miss, const std::set<uint64_t>& wait_
             !sb_cuda_ok(cudaStreamWaitEvent(g_rt.copy, g_res.done[r], 0), "copy stream wait"))
             return false;
     }
-    // pinned sources by direct DMA; pageable or file-mapped ones through the
-    // pinned staging ring and its reader lanes (sb_staging.cu)
+    // bytes a readahead already holds (or is reading) are copied from its
+    // buffer; pinned sources by direct DMA; pageable or file-mapped ones through
+    // the pinned staging ring and its reader lanes (sb_staging.cu)
     std::vector<sb_fill> fills;
     fills.reserve(miss.size());
-    for (const Fetch& f : miss) fills.push_back({f.dst, f.src, f.bytes});
+    const bool pf = sb_pf_enabled();
+    for (const Fetch& f : miss)
+        if (!(pf && sb_pf_take(f.src, f.bytes, f.dst, g_rt.copy))) fills.push_back({f.dst, f.src, f.bytes});
     if (!fills.empty() && !sb_stage_fill(fills.data(), (int)fills.size(), g_rt.copy)) return false;
     for (const Fetch& f : miss) {
         auto it = g_res.map.find(Key{f.src_key, f.expert, f.bytes, f.shape});
@@ -643,7 +649,10 @@ int snapshot_json(char* buf, size_t n) {
         "\"selfcheck_multi_token\":%llu,\"selfcheck_tensors\":%llu,\"selfcheck_slots\":[%s],"
         "\"sentinel\":%d,\"device_calls\":%llu,\"id_reuse\":%llu,"
         "\"staged_bytes\":%llu,\"pinned_fill_bytes\":%llu,\"direct_io_reads\":%llu,\"direct_io_bytes\":%llu,"
-        "\"direct_io_fallbacks\":%llu,\"fill_waves\":%llu,\"merged_slots\":%llu}",
+        "\"direct_io_fallbacks\":%llu,\"fill_waves\":%llu,\"merged_slots\":%llu,"
+        "\"prefetch_enabled\":%d,\"prefetch_reads\":%llu,\"prefetch_read_bytes\":%llu,\"prefetch_used\":%llu,"
+        "\"prefetch_used_bytes\":%llu,\"prefetch_dropped\":%llu,\"prefetch_stale\":%llu,\"prefetch_waits\":%llu,"
+        "\"prefetch_wait_ms\":%.3f,\"prefetch_wait_timeouts\":%llu}",
         (unsigned long long)g_res.calls, (unsigned long long)g_res.empty_calls, (unsigned long long)g_res.tokens,
         (unsigned long long)(g_res.hits + g_res.misses), (unsigned long long)g_res.hits,
         (unsigned long long)g_res.misses, (unsigned long long)g_res.evictions,
@@ -654,13 +663,14 @@ int snapshot_json(char* buf, size_t n) {
         (unsigned long long)g_res.sc_tensors.size(), slots, SABAH_SENTINEL,
         (unsigned long long)g_res.device_calls, (unsigned long long)g_res.id_reuse, ss.staged_bytes, ss.pinned_bytes,
         ss.direct_io_reads, ss.direct_io_bytes, ss.direct_io_fallbacks, ss.waves,
-        (unsigned long long)g_chain.merged_slots);
+        (unsigned long long)g_chain.merged_slots, sb_pf_enabled() ? 1 : 0, ss.pf_reads, ss.pf_read_bytes, ss.pf_used,
+        ss.pf_used_bytes, ss.pf_dropped, ss.pf_stale, ss.pf_waits, (double)ss.pf_wait_ns / 1e6, ss.pf_wait_timeouts);
 }
 
 void status_write() {
     static const char* path = std::getenv("SABAH_LLAMA_STATUS_FILE");
     if (!path || !*path) return;
-    char buf[1024];
+    char buf[2048];
     snapshot_json(buf, sizeof(buf));
     if (FILE* f = std::fopen(path, "wb")) {
         std::fputs(buf, f);
@@ -671,7 +681,7 @@ void status_write() {
 
 void report_at_exit() {
     if (!std::getenv("SABAH_LLAMA_TRACE")) return;
-    char buf[1024];
+    char buf[2048];
     snapshot_json(buf, sizeof(buf));
     std::fprintf(stderr, "SABAH_DIAG calls=%llu tokens=%llu lookups=%llu overflow=%llu verify_ok=%llu verify_fail=%llu\n",
                  (unsigned long long)g_res.calls, (unsigned long long)g_res.tokens,
@@ -1297,6 +1307,23 @@ SABAH_API int sabah_rt_mul_mat_id_v2(const void* source, size_t expert_stride, s
                                      wait_epochs))
                         return -1;
                     g_chain.merged_slots += miss.size() - before;
+                }
+                f = l.next;
+            }
+        } else if (sb_pf_enabled() && n_tokens <= kPfMaxTokens) {
+            // staging readahead (ref sabah_rt.cu:1517-1860): the followers' experts
+            // that the tier does not hold are read into pinned buffers now, while
+            // this call's fill and kernel run; their calls take the bytes from there
+            const void* f = source;
+            for (int depth = 0; depth < 2; ++depth) {
+                auto li = g_chain.links.find(f);
+                if (li == g_chain.links.end() || !li->second.shares_ids || !li->second.next) break;
+                const ChainLink l = li->second;
+                std::set<int32_t> distinct(ids_now.begin(), ids_now.end());
+                for (int32_t e : distinct) {
+                    if (e < 0 || e >= l.n_experts) continue;
+                    if (g_res.map.count(Key{l.next, e, l.stride, l.shape})) continue;   // resident already
+                    sb_pf_offer((const uint8_t*)l.next + (size_t)e * l.stride, l.stride);
                 }
                 f = l.next;
             }

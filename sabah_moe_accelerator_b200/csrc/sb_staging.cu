@@ -26,12 +26,26 @@
 // The caller (the residency code in sb_runtime.cu) holds the residency lock,
 // records the copy stream's completion event after sb_stage_fill returns, and
 // makes the compute stream wait on it, as for direct copies.
+//
+// Staging readahead (SABAH_LLAMA_PREFETCH=1, off by default as in the
+// reference, sabah_rt.cu:1517-1860): a layer's gate, up and down calls read the
+// same router ids, so when the first of them has its ids, the experts the other
+// two will miss are known. The residency code offers those experts here; 8
+// reader threads read each into a pinned readahead buffer of its own (O_DIRECT
+// from the file where the source is file-mapped). The bytes stay there: nothing
+// is reserved in the hot tier, so a wrong guess costs a read and no slot. When
+// the follower call misses the expert, sb_pf_take queues the copy straight from
+// that buffer (waiting up to 50 ms for a read still in flight rather than
+// reading the same bytes twice), and the buffer is reused once that copy has
+// landed. With every buffer busy, an offer replaces the oldest unclaimed
+// readahead, or is dropped.
 #include <fcntl.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
@@ -286,6 +300,240 @@ bool sb_stage_fill(const sb_fill* f, int n, cudaStream_t copy) {
     return true;
 }
 
+// ------------------------------------------------------------ staging readahead
+namespace {
+
+constexpr int kPfBuffers = 8;          // readahead buffers = reads in flight
+constexpr size_t kPfMaxQueue = 64;
+constexpr int kPfWaitMs = 50;
+
+enum PfState { kPfFree, kPfFilling, kPfReady, kPfTaken, kPfFail };
+
+struct PfBuffer {
+    uint8_t* raw = nullptr;
+    uint8_t* mem = nullptr;        // pinned, kAlign-aligned
+    size_t cap = 0;                // usable bytes at mem
+    size_t delta = 0;              // the expert's bytes start at mem + delta
+    int state = kPfFree;
+    const void* src = nullptr;     // identity: the expert's host bytes
+    size_t bytes = 0;
+    uint64_t seq = 0;
+    cudaEvent_t free_ev = nullptr; // recorded after the copy out of this buffer
+    bool free_pending = false;
+};
+
+struct PfJob {
+    int buf;
+    const uint8_t* src;
+    size_t bytes;
+};
+
+struct Prefetcher {
+    std::mutex mu;
+    std::condition_variable cv_work, cv_done;
+    std::deque<PfJob> queue;
+    PfBuffer buf[kPfBuffers];
+    std::vector<std::thread> readers;
+    bool stop = false;
+    int device = 0;
+    uint64_t seq = 0;
+    unsigned long long reads = 0, read_bytes = 0, used = 0, used_bytes = 0, dropped = 0, stale = 0, waits = 0,
+                       wait_ns = 0, wait_timeouts = 0;
+    ~Prefetcher() {
+        {
+            std::lock_guard<std::mutex> l(mu);
+            stop = true;
+        }
+        cv_work.notify_all();
+        for (std::thread& t : readers)
+            if (t.joinable()) t.join();
+    }
+};
+Prefetcher g_pf;
+
+bool pf_env_on() {
+    static int on = -1;
+    if (on < 0) {
+        const char* v = std::getenv("SABAH_LLAMA_PREFETCH");
+        on = v && *v && std::strcmp(v, "0") != 0 && std::strcmp(v, "off") != 0;
+    }
+    return on != 0;
+}
+
+// Room for `need` bytes, and no copy still reading the buffer. Reader thread,
+// while the buffer is kPfFilling (nobody else touches it then).
+bool pf_prepare(PfBuffer& b, size_t need) {
+    if (b.free_pending) {
+        if (cudaEventSynchronize(b.free_ev) != cudaSuccess) return false;
+        b.free_pending = false;
+    }
+    if (b.cap < need) {
+        if (b.raw) cudaFreeHost(b.raw);
+        b.raw = b.mem = nullptr;
+        b.cap = 0;
+        if (cudaHostAlloc((void**)&b.raw, need + kAlign, cudaHostAllocDefault) != cudaSuccess) return false;
+        b.mem = (uint8_t*)(((uintptr_t)b.raw + kAlign - 1) & ~(uintptr_t)(kAlign - 1));
+        b.cap = need;
+    }
+    return true;
+}
+
+// One expert into its buffer: an O_DIRECT read of the covering aligned range
+// when the bytes lie in a file mapping and direct I/O is on, else a copy from
+// the source.
+bool pf_read(PfBuffer& b, const uint8_t* src, size_t bytes) {
+    if (direct_io_on()) {
+        Mapping m;
+        if (mapping_of(src, bytes, m) && m.fd >= 0) {
+            const uint64_t off = m.off + ((uintptr_t)src - m.lo);
+            const uint64_t base = off & ~(uint64_t)(kAlign - 1);
+            const size_t delta = (size_t)(off - base);
+            const size_t len = (delta + bytes + kAlign - 1) & ~(kAlign - 1);
+            if (!pf_prepare(b, len)) return false;
+            const ssize_t got = ::pread(m.fd, b.mem, len, (off_t)base);
+            if (got >= (ssize_t)(delta + bytes)) {
+                b.delta = delta;
+                ++g_st.dio_reads;
+                g_st.dio_bytes += bytes;
+                return true;
+            }
+            ++g_st.dio_fallbacks;
+        }
+    }
+    if (!pf_prepare(b, bytes)) return false;
+    std::memcpy(b.mem, src, bytes);
+    b.delta = 0;
+    return true;
+}
+
+void pf_reader() {
+    cudaSetDevice(g_pf.device);
+    for (;;) {
+        PfJob j;
+        {
+            std::unique_lock<std::mutex> l(g_pf.mu);
+            g_pf.cv_work.wait(l, [] { return g_pf.stop || !g_pf.queue.empty(); });
+            if (g_pf.stop) return;
+            j = g_pf.queue.front();
+            g_pf.queue.pop_front();
+        }
+        PfBuffer& b = g_pf.buf[j.buf];
+        const bool ok = pf_read(b, j.src, j.bytes);
+        {
+            std::lock_guard<std::mutex> l(g_pf.mu);
+            b.state = ok ? kPfReady : kPfFail;
+            if (ok) {
+                ++g_pf.reads;
+                g_pf.read_bytes += j.bytes;
+            }
+        }
+        g_pf.cv_done.notify_all();   // a miss may be waiting for this buffer
+    }
+}
+
+void pf_start_locked() {
+    if (!g_pf.readers.empty()) return;
+    cudaGetDevice(&g_pf.device);
+    g_pf.stop = false;
+    for (int i = 0; i < kPfBuffers; ++i) g_pf.readers.emplace_back(pf_reader);
+}
+
+}  // namespace
+
+bool sb_pf_enabled() { return pf_env_on(); }
+
+void sb_pf_offer(const void* src, size_t bytes) {
+    if (!pf_env_on() || !src || bytes == 0 || is_pinned(src)) return;
+    std::lock_guard<std::mutex> l(g_pf.mu);
+    pf_start_locked();
+    if (g_pf.queue.size() >= kPfMaxQueue) return;
+    int pick = -1;
+    for (int i = 0; i < kPfBuffers; ++i) {
+        const PfBuffer& b = g_pf.buf[i];
+        if ((b.state == kPfReady || b.state == kPfFilling) && b.src == src && b.bytes == bytes) return;
+        if (pick < 0 && (b.state == kPfFree || b.state == kPfFail)) pick = i;
+    }
+    if (pick < 0) {   // every buffer busy: the oldest readahead nobody has claimed
+        uint64_t oldest = ~0ull;
+        for (int i = 0; i < kPfBuffers; ++i)
+            if (g_pf.buf[i].state == kPfReady && g_pf.buf[i].seq < oldest) {
+                oldest = g_pf.buf[i].seq;
+                pick = i;
+            }
+        if (pick < 0) {
+            ++g_pf.dropped;
+            return;
+        }
+        ++g_pf.stale;
+    }
+    PfBuffer& b = g_pf.buf[pick];
+    b.state = kPfFilling;
+    b.src = src;
+    b.bytes = bytes;
+    b.seq = ++g_pf.seq;
+    g_pf.queue.push_back({pick, (const uint8_t*)src, bytes});
+    g_pf.cv_work.notify_one();
+}
+
+bool sb_pf_take(const void* src, size_t bytes, void* dst, cudaStream_t copy) {
+    if (!pf_env_on()) return false;
+    int idx = -1;
+    bool waited = false;
+    const auto t0 = std::chrono::steady_clock::now();
+    const auto deadline = t0 + std::chrono::milliseconds(kPfWaitMs);
+    {
+        std::unique_lock<std::mutex> l(g_pf.mu);
+        for (;;) {
+            int found = -1;
+            for (int i = 0; i < kPfBuffers; ++i) {
+                PfBuffer& b = g_pf.buf[i];
+                if (b.src != src || b.bytes != bytes) continue;
+                if (b.state == kPfFail) {   // the read failed: the miss is staged as usual
+                    b.state = kPfFree;
+                    b.src = nullptr;
+                    return false;
+                }
+                if (b.state == kPfReady || b.state == kPfFilling) {
+                    found = i;
+                    break;
+                }
+            }
+            if (found < 0) return false;
+            if (g_pf.buf[found].state == kPfReady) {
+                g_pf.buf[found].state = kPfTaken;
+                idx = found;
+                break;
+            }
+            // still reading: wait for it rather than read the same bytes twice
+            waited = true;
+            if (g_pf.cv_done.wait_until(l, deadline) == std::cv_status::timeout) {
+                ++g_pf.wait_timeouts;
+                return false;
+            }
+        }
+        if (waited) {
+            ++g_pf.waits;
+            g_pf.wait_ns += (unsigned long long)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                std::chrono::steady_clock::now() - t0)
+                                .count();
+        }
+    }
+    PfBuffer& b = g_pf.buf[idx];
+    bool ok = b.free_ev || cudaEventCreateWithFlags(&b.free_ev, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && sb_cuda_ok(cudaMemcpyAsync(dst, b.mem + b.delta, bytes, cudaMemcpyHostToDevice, copy),
+                          "readahead expert H2D") &&
+         sb_cuda_ok(cudaEventRecord(b.free_ev, copy), "readahead free record");
+    std::lock_guard<std::mutex> l(g_pf.mu);
+    b.free_pending = ok;   // the next read into this buffer waits for the copy out
+    b.state = kPfFree;
+    b.src = nullptr;
+    if (ok) {
+        ++g_pf.used;
+        g_pf.used_bytes += bytes;
+    }
+    return ok;
+}
+
 void sb_stage_stats_get(sb_stage_stats* s) {
     s->staged_bytes = g_st.staged_bytes;
     s->pinned_bytes = g_st.pinned_bytes;
@@ -293,9 +541,36 @@ void sb_stage_stats_get(sb_stage_stats* s) {
     s->direct_io_bytes = g_st.dio_bytes;
     s->direct_io_fallbacks = g_st.dio_fallbacks;
     s->waves = g_st.waves;
+    std::lock_guard<std::mutex> l(g_pf.mu);
+    s->pf_reads = g_pf.reads;
+    s->pf_read_bytes = g_pf.read_bytes;
+    s->pf_used = g_pf.used;
+    s->pf_used_bytes = g_pf.used_bytes;
+    s->pf_dropped = g_pf.dropped;
+    s->pf_stale = g_pf.stale;
+    s->pf_waits = g_pf.waits;
+    s->pf_wait_ns = g_pf.wait_ns;
+    s->pf_wait_timeouts = g_pf.wait_timeouts;
 }
 
 void sb_stage_shutdown() {
+    {   // the readahead: readers stopped, buffers released once their copies landed
+        {
+            std::lock_guard<std::mutex> l(g_pf.mu);
+            g_pf.stop = true;
+        }
+        g_pf.cv_work.notify_all();
+        for (std::thread& t : g_pf.readers) t.join();
+        std::lock_guard<std::mutex> l(g_pf.mu);
+        g_pf.readers.clear();
+        g_pf.queue.clear();
+        for (PfBuffer& b : g_pf.buf) {
+            if (b.free_ev) cudaEventSynchronize(b.free_ev), cudaEventDestroy(b.free_ev);
+            if (b.raw) cudaFreeHost(b.raw);
+            b = PfBuffer{};
+        }
+        g_pf.stop = false;
+    }
     {
         std::lock_guard<std::mutex> l(g_st.mu);
         g_st.stop = true;

@@ -117,6 +117,27 @@ def test_merged_layer_fetch_fills_followers_in_one_wave(tmp_path):
     assert off["out_sha"] == r["out_sha"], "merged and per-call fetches gave different results"
 
 
+def test_staging_readahead_serves_the_followers(tmp_path):
+    """SABAH_LLAMA_PREFETCH=1 (ref sabah_rt.cu:1517-1860, 2051-2065): token 1
+    teaches the runtime the call chain; on token 2 the gate call offers the up
+    and down experts the tier lacks, reader threads read them from the file
+    into pinned readahead buffers, and the follower calls' misses copy from
+    there instead of reading the file again. Nothing is reserved in the tier:
+    the followers still count their misses. Every output stays exact and
+    byte-verified, and equal to the run without readahead."""
+    r = _child("layer", tmp_path, {"SABAH_LLAMA_PREFETCH": "1", "SABAH_LLAMA_LAYER_MERGE": "0"})
+    assert r["rel"] <= TIGHT, r
+    s = r["snapshot"]
+    assert s["verify_fail"] == 0 and s["verify_ok"] > 0, s
+    assert s["prefetch_enabled"] == 1 and s["merged_slots"] == 0, s
+    assert s["prefetch_reads"] > 0 and s["prefetch_used"] > 0, s
+    assert s["prefetch_used_bytes"] <= s["prefetch_read_bytes"], s
+    assert r["follower_misses_token2"] > 0, r
+    off = _child("layer", tmp_path, {"SABAH_LLAMA_PREFETCH": "0", "SABAH_LLAMA_LAYER_MERGE": "0"})
+    assert off["snapshot"]["prefetch_enabled"] == 0 and off["snapshot"]["prefetch_used"] == 0, off
+    assert off["out_sha"] == r["out_sha"], "readahead and plain fetches gave different results"
+
+
 _CHILD_LAYER = r"""
 import hashlib, json, os, sys
 import numpy as np, torch

@@ -621,8 +621,8 @@ int sb_try_mmid_q8_0(const sb_mmid_args& a, cudaStream_t st) {
 
 int sb_try_block_iq3s(const sb_block_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !fast_path_enabled()) return 0;
-    if (!a.xrows) {   // the grouped path reads rows t only
-        const int grouped = sb_block_iq3s_grouped(a, st);   // many (token, slot) pairs
+    {   // many (token, slot) pairs; gathered input rows are copied into place first
+        const int grouped = sb_block_iq3s_grouped(a, st);
         if (grouped != 0) return grouped;
     }
     // one persistent launch (sb_decode_iq3s.cu, one block): every combine is CTA-local,

@@ -1132,7 +1132,10 @@ BlockGroupedScratch g_bgs;
 // IQ3_S experts, uniform routing, 64 and 512 experts, 1-1024 pairs): the
 // one-launch path costs ~20 us plus ~1.1 us a pair with one slot per token
 // (32-row down items) and ~1.4 us a pair otherwise; the grouped path ~145 us
-// plus ~2 us per distinct expert and 8-pair task, with the distinct experts of
+// plus ~1.5 us per distinct expert and 8-pair task (refitted after the
+// register-decode kernel moved to 16 warps and to the tcgen05 kernel's tail:
+// 640 one-slot pairs over 512 experts take 691 us grouped, 698 us in one
+// launch, and the whole expert-parallel step gains 7.6%), with the distinct experts of
 // P uniformly routed pairs over E expected at E (1 - exp(-P / E)). The ids are
 // on the device, so the expectation stands in for the count.
 bool block_grouped_wins(long long pairs, int n_experts, int n_used) {
@@ -1145,10 +1148,27 @@ bool block_grouped_wins(long long pairs, int n_experts, int n_used) {
     const double P = (double)pairs, E = (double)std::max(1, n_experts);
     const double distinct = E * (1.0 - std::exp(-P / E));
     const double tasks = distinct * std::max(1.0, std::ceil(P / distinct / 8.0));
-    return 145.0 + 2.0 * tasks < (n_used == 1 ? 20.0 + 1.1 * P : 1.4 * P);
+    return 145.0 + 1.5 * tasks < (n_used == 1 ? 20.0 + 1.1 * P : 1.4 * P);
 }
 
 }  // namespace
+
+// Token t's input row xrows[t] of x into dst row t; a row index outside
+// [0, n_xrows) gives a NaN row and SB_DERR_BAD_ID, as in the one-launch path.
+__global__ void k_rows_gather(const float4* x, int n_xrows, const int32_t* xrows, int n, int k4, float4* dst, int* err) {
+    const long long total = (long long)n * k4;
+    for (long long q = blockIdx.x * (long long)blockDim.x + threadIdx.x; q < total; q += (long long)gridDim.x * blockDim.x) {
+        const int i = (int)(q / k4), j = (int)(q % k4);
+        const int r = __ldg(xrows + i);
+        if (r < 0 || r >= n_xrows) {
+            const float f = __int_as_float(0x7fc00000);
+            if (err && j == 0) atomicExch(err, SB_DERR_BAD_ID);
+            dst[q] = make_float4(f, f, f, f);
+        } else {
+            dst[q] = __ldg(x + (size_t)r * k4 + j);
+        }
+    }
+}
 
 int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st) {
     if (a.qt_gate != SB_IQ3_S || a.qt_up != SB_IQ3_S || a.qt_down != SB_IQ3_S || !prefill_enabled()) return 0;
@@ -1160,7 +1180,9 @@ int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st) {
         if (((uintptr_t)e->base & 15) || e->expert_stride % 16) return 0;
     if (((uintptr_t)a.x & 15) || ((uintptr_t)a.h & 15) || ((uintptr_t)a.out & 3)) return 0;
 
-    const size_t need = (size_t)slots * (2 * a.ff + a.d_model);
+    // gathered inputs (token t reads row xrows[t]) are copied into place first
+    const size_t gathered = a.xrows ? (size_t)a.n_tokens * a.d_model : 0;
+    const size_t need = (size_t)slots * (2 * a.ff + a.d_model) + gathered;
     if (need > g_bgs.cap) {
         if (g_bgs.mem) {
             cudaDeviceSynchronize();   // no kernel of an earlier call may still use it
@@ -1173,10 +1195,18 @@ int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st) {
     float* gout = g_bgs.mem;
     float* uout = gout + slots * a.ff;
     float* dout = uout + slots * a.ff;
+    const float* x = a.x;
+    if (a.xrows) {
+        float* xg = dout + slots * a.d_model;
+        const long long n4 = (long long)a.n_tokens * (a.d_model / 4);
+        k_rows_gather<<<(int)std::min<long long>((n4 + 255) / 256, 148LL * 8), 256, 0, st>>>(
+            (const float4*)a.x, a.n_xrows, a.xrows, a.n_tokens, a.d_model / 4, (float4*)xg, a.err);
+        x = xg;
+    }
 
     sb_mmid_args m{};
     m.row_stride = sb_row_bytes_of(SB_IQ3_S, a.d_model);
-    m.x = a.x;
+    m.x = x;
     m.x_id_stride = (size_t)a.d_model * 4;
     m.x_rows = 1;
     m.x_token_stride = (size_t)a.d_model * 4;

@@ -419,13 +419,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_flow_iq3s(const __grid_constant
                 }
             }
             if (!ok || nd == 0) continue;
-            // every task of the unit is done: super-blocks in order, slots in order (weighted)
-            float tot = 0.f;
-            for (int e2 = 0; e2 < p.n_used; ++e2) {
-                float v = 0.f;
-                for (int j2 = 0; j2 < spr; ++j2) v += dred[(e2 * spr + j2) * 16 + r];
-                tot += __shfl_sync(0xffffffffu, wl, e2) * v;
+            // every task of the unit is done: super-blocks in order, slots in order
+            // (weighted). The combine lies on the layer's critical path (the next
+            // layer's gate/up waits for x), so half hf of the warp sums half of
+            // the slots and the halves are added, first half first
+            const int half = (p.n_used + 1) / 2;
+            const int e_lo = hf ? half : 0, e_hi = hf ? p.n_used : half;
+            float part = 0.f;
+            for (int e2 = 0; e2 < (p.n_used + 1) / 2; ++e2) {
+                const int e = e_lo + e2;
+                const float we = __shfl_sync(0xffffffffu, wl, min(e, 31));
+                if (e < e_hi) {
+                    float v = 0.f;
+                    for (int j2 = 0; j2 < spr; ++j2) v += dred[(e * spr + j2) * 16 + r];
+                    part += we * v;
+                }
             }
+            const float other = __shfl_xor_sync(0xffffffffu, part, 16);
+            const float tot = hf ? other + part : part + other;
             xr = xr + tot;
             __syncwarp();   // dred is read before the next layer's tasks may write it
             if (lane < 16) {

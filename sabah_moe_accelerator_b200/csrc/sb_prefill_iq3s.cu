@@ -503,7 +503,7 @@ struct GroupParams {
                       // most kGMaxPairs): {expert, -, first pair, pairs}; a task is (entry,
                       // 128-row block), task index = entry * m_tiles + block
     int* n_mtasks;    // entries * m_tiles
-    int* mnext;       // the register-decode kernel's next task (zeroed by the plan)
+    int* mnext;       // the register-decode kernel's next task, [0] and [4] (zeroed by the plan)
     int heavy;
     int* order;       // [pairs] pair index in grouped order
     PairInfo* pairs;  // [pairs] grouped order
@@ -573,7 +573,8 @@ __global__ void k_group_plan(const GroupParams g) {
     if (threadIdx.x == 1023) {
         *g.n_tasks = s_tsum[1023];
         *g.n_mtasks = s_msum[1023] * g.m_tiles;
-        *g.mnext = 0;
+        g.mnext[0] = 0;
+        g.mnext[4] = 0;   // the counter of a second run over the same plan (the block's up call)
     }
 }
 
@@ -964,7 +965,18 @@ int sb_prefill_min_pairs() {
     return v;
 }
 
+namespace {
+// The kernel parameters of the last grouped call, for a second run over the
+// same plan (the fused block's up call: same ids, x, rows and k as its gate call)
+struct LastPlan {
+    GemmParams gp;
+    MmaParams mp;
+    bool valid = false;
+} g_last_plan;
+}  // namespace
+
 int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force) {
+    g_last_plan.valid = false;
     if (a.qt != SB_IQ3_S || !prefill_enabled() || a.ex.ptrs) return 0;
     const long long n_pairs = (long long)a.n_ids * a.n_tokens;
     if ((!force && n_pairs < sb_prefill_min_pairs()) || n_pairs < 1 || n_pairs > (1 << 24)) return 0;
@@ -1094,8 +1106,42 @@ int sb_try_mmid_iq3s_grouped(const sb_mmid_args& a, cudaStream_t st, bool force)
         if (!sb_cuda_ok(cudaLaunchKernelEx(&cfg, k_group_mma_iq3s, mp), "grouped mma launch")) return -1;
     }
     sb_timing_end(tslot, st);
+    g_last_plan.gp = gp;
+    g_last_plan.mp = mp;
+    g_last_plan.valid = true;
     return sb_cuda_ok(cudaGetLastError(), "prefill launch") ? 1 : -1;
 }
+
+namespace {
+// The last grouped call's two kernels again, over its plan and split x, for
+// another bank of the same geometry into another output of the same strides.
+// The plan's pair order, tasks and x rows depend only on the ids, x and the
+// shapes, so none of the grouping kernels runs again.
+int grouped_rerun(const uint8_t* base, size_t expert_stride, uint8_t* dst, cudaStream_t st) {
+    if (!g_last_plan.valid || expert_stride != g_last_plan.gp.expert_stride) return 0;
+    GemmParams gp = g_last_plan.gp;
+    MmaParams mp = g_last_plan.mp;
+    gp.base = mp.base = base;
+    gp.dst = mp.dst = dst;
+    mp.next = g_last_plan.mp.next + 4;   // the second counter, zeroed by the plan
+    g_last_plan.valid = false;           // one rerun per plan: the second counter is spent
+    const int tslot = sb_timing_begin("prefill_iq3s", st);
+    k_prefill_iq3s<<<g_grid, kThreads, Smem::total, st>>>(gp);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(g_grid);
+    cfg.blockDim = dim3(kGThreads);
+    cfg.dynamicSmemBytes = MmaSmem::total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (!sb_cuda_ok(cudaLaunchKernelEx(&cfg, k_group_mma_iq3s, mp), "grouped mma launch")) return -1;
+    sb_timing_end(tslot, st);
+    return sb_cuda_ok(cudaGetLastError(), "prefill launch") ? 1 : -1;
+}
+}  // namespace
 
 // ------------------------------------------------------------ the fused block, grouped
 namespace {
@@ -1221,9 +1267,14 @@ int sb_block_iq3s_grouped(const sb_block_args& a, cudaStream_t st) {
     m.ex = a.gate;
     m.dst = gout;
     if (sb_try_mmid_iq3s_grouped(m, st, true) != 1) return -1;
-    m.ex = a.up;
-    m.dst = uout;
-    if (sb_try_mmid_iq3s_grouped(m, st, true) != 1) return -1;
+    // up: the gate call's plan and split x again (same ids, x and shapes)
+    const int rerun = grouped_rerun(a.up.base, a.up.expert_stride, (uint8_t*)uout, st);
+    if (rerun < 0) return -1;
+    if (rerun == 0) {
+        m.ex = a.up;
+        m.dst = uout;
+        if (sb_try_mmid_iq3s_grouped(m, st, true) != 1) return -1;
+    }
     const long long nh = slots * a.ff;
     const int tslot = sb_timing_begin("block_grouped_elementwise", st);
     k_swiglu<<<(int)std::min<long long>((nh + 255) / 256, 148LL * 8), 256, 0, st>>>(gout, uout, a.h, nh);

@@ -835,6 +835,33 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
     L.sabah_rt_kernel_times(buf, 8192)
     L.sabah_rt_kernel_timing(0)
     ktimes = json.loads(buf.value.decode())
+    # e2e: per step the tokens' x rows and router ids from pinned host memory,
+    # the three v2 calls (C ABI), the down call's output rows back to pinned
+    # host memory (h, the down call's input, stays on the device as the SwiGLU
+    # between the calls would leave it)
+    x_h = x.cpu().pin_memory()
+    ids_h = [t.cpu().pin_memory() for t in ids_d]
+    out_h = torch.empty(tuple(d_out.shape), dtype=torch.float32).pin_memory()
+    x_e, ids_e = torch.empty_like(x), torch.empty_like(ids_d[0])
+
+    def e2e_step(s):
+        x_e.copy_(x_h, non_blocking=True)
+        ids_e.copy_(ids_h[s], non_blocking=True)
+        ops.mul_mat_id(gate, GU_EXPERT, GU_ROW, x_e, ids_e, FF, D_MODEL, EXPERTS, QT_IQ3_S, out=g_out, stream=stream)
+        ops.mul_mat_id(up, GU_EXPERT, GU_ROW, x_e, ids_e, FF, D_MODEL, EXPERTS, QT_IQ3_S, out=u_out, stream=stream)
+        ops.mul_mat_id(down, D_EXPERT, D_ROW, h, ids_e, D_MODEL, FF, EXPERTS, QT_IQ3_S, out=d_out, stream=stream)
+        out_h.copy_(d_out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(2, min(args.warmup, 3))):
+            e2e_step(i % PF_SETS)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            e2e_step(i % PF_SETS)
+        e1.record(stream)
+    stream.synchronize()
+    e_ms = e0.elapsed_time(e1) / args.steps
     distinct = np.mean([np.unique(ids_np[s]).size for s in range(PF_SETS)])
     alg_bytes = distinct * (2 * GU_EXPERT + D_EXPERT) + T * D_MODEL * 4 + 2 * T * K * FF * 4 * 2 + T * K * D_MODEL * 4
     flops = 2.0 * T * K * (2 * FF * D_MODEL + D_MODEL * FF)
@@ -857,6 +884,11 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
                                 "note": "algorithmic FLOPs; the kernel issues 3 fp16 MMAs per product (hi/lo split)"},
                      "kernels": {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / v[0], 2)}
                                  for k, v in ktimes.items()}},
+        "e2e": {"value": round(T * 1e3 / e_ms, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x_h.numel() * 4 + ids_h[0].numel() * 4),
+                "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
+                "path": "sabah_rt_mul_mat_id_v2 (C ABI) x3 per step; x and ids from pinned host memory, "
+                        "the down output rows back"},
         "gpu_launches": int(sum(v[0] for v in ktimes.values()) * args.steps),
         "clocks": clk,
         "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3,

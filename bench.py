@@ -46,7 +46,7 @@ WORKLOAD = "cfg2: IQ3_S decode, 1 token x 48 blocks, 512 experts/block, top-10, 
 # DRAM bytes (read + write) per decoded block of the persistent decode kernels,
 # from one ncu capture each on the 2-block case (profiles/), keyed by the
 # runtime's kernel-timing name
-DRAM_BYTES_PER_BLOCK = {"decode_iq3s": (40.62e6 + 0.27e6) / 2, "decode_iq3s_flow": (40.88e6 + 0.24e6) / 2}
+DRAM_BYTES_PER_BLOCK = {"decode_iq3s": (40.62e6 + 0.27e6) / 2, "decode_iq3s_flow": (40.905728e6 + 0.135936e6) / 2}
 
 
 def iq3s_row_bytes(k: int) -> int:

@@ -451,6 +451,45 @@ def cpu_baseline(bank, gate_p, up_p, down_p, ids_np, w_np, use_ref: bool, n_laye
                 n_layers, reps)}
 
 
+def cpu_baseline_mixed(gate_p, up_p, down_p, ids_np, w_np, x0_np, n_layers: int = 2):
+    """cfg 4's CPU baseline: the oracle's fp32 decode (Q4_K gate/up, Q6_K down)
+    of the step's tokens, each through the first n_layers blocks of routing
+    set 0, all host threads; scaled to the 48-block step. Only the sampled
+    blocks' distinct experts are copied to the host."""
+    from oracle import cpu as orc
+    from sabah_moe_accelerator_b200 import rt
+    d2h = rt.lib().sabah_memcpy_d2h
+    T = ids_np.shape[2]
+    banks, local = [], np.zeros((T, n_layers, TOP_K), np.int32)
+    for Lr in range(n_layers):
+        sel = np.unique(ids_np[0, Lr])
+        g = np.empty((len(sel), MX_GU_EXPERT), np.uint8)
+        u = np.empty((len(sel), MX_GU_EXPERT), np.uint8)
+        d = np.empty((len(sel), MX_D_EXPERT), np.uint8)
+        for j, e in enumerate(sel):
+            for arr, base, stride in ((g, gate_p[Lr], MX_GU_EXPERT), (u, up_p[Lr], MX_GU_EXPERT),
+                                      (d, down_p[Lr], MX_D_EXPERT)):
+                rt.check(d2h(arr[j].ctypes.data, base + int(e) * stride, stride), "sample copy")
+        banks.append((g, u, d))
+        for t in range(T):
+            local[t, Lr] = np.searchsorted(sel, ids_np[0, Lr, t])
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for t in range(T):
+            orc.decode_f32([b[0].ctypes.data for b in banks], [b[1].ctypes.data for b in banks],
+                           [b[2].ctypes.data for b in banks], MX_GU_EXPERT, MX_D_EXPERT, QT_Q4_K, QT_Q6_K,
+                           local[t], w_np[0, :n_layers, t], x0_np[t], D_MODEL, FF, threads)
+        reps += 1
+        if time.perf_counter() - t0 > 10.0 or reps >= 10:
+            break
+    per_step = (time.perf_counter() - t0) / reps * LAYERS / n_layers
+    return {"value": round(T / per_step, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": "the %d tokens of routing set 0 through %d of 48 blocks, %d repetitions, scaled to 48 blocks"
+                      % (T, n_layers, reps)}
+
+
 # ---------------------------------------------------------------------------
 # reference arm: the reference's own CPU path (its host dequantizer, compiled
 # from its sources into oracle/_ref) + fp32 dots, all host threads. Nothing of
@@ -1498,6 +1537,7 @@ def run_mixed(args, rank: int, world: int, local_rank: int):
     e_ms = e0.elapsed_time(e1) / e2e_steps
     assert np.isfinite(out_h.numpy()).all(), "non-finite decode output"
     del graphs
+    cpu = None if args.no_cpu_baseline else cpu_baseline_mixed(gate_p, up_p, down_p, ids_np, w_np, x0_np)
     return {
         "metric": MX_METRIC, "value": round(T * 1e3 / ms, 2), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -1514,6 +1554,7 @@ def run_mixed(args, rank: int, world: int, local_rank: int):
                 "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
                 "path": "sabah_moe_decode (C ABI), eager launches"},
         "gpu_launches": int(round(launches_per_step * args.steps)),
+        "cpu_baseline": cpu,
         "clocks": clk,
         "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3,
                    "checked": "routing set 0, all %d blocks, every token (worst), before timing" % LAYERS}

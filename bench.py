@@ -451,6 +451,38 @@ def cpu_baseline(bank, gate_p, up_p, down_p, ids_np, w_np, use_ref: bool, n_laye
                 n_layers, reps)}
 
 
+def cpu_baseline_prefill(gate, up, down, ids_np, x_np, n_tok: int = 8):
+    """cfg 3's CPU baseline: the oracle's fp32 block (gate, up, SwiGLU, down,
+    combine: one token's three MUL_MAT_ID rows of work) for a sample of the
+    step's tokens, all host threads; tokens/s. Only the sample's routed experts
+    are copied to the host."""
+    from oracle import cpu as orc
+    toks = np.random.default_rng(25).choice(ids_np.shape[1], n_tok, replace=False)
+    sel = np.unique(ids_np[0, toks])
+    g = np.empty((len(sel), GU_EXPERT), np.uint8)
+    u = np.empty((len(sel), GU_EXPERT), np.uint8)
+    down_h = np.empty((len(sel), D_EXPERT), np.uint8)
+    for j, e in enumerate(sel):
+        g[j] = gate[int(e) * GU_EXPERT:(int(e) + 1) * GU_EXPERT].cpu().numpy()
+        u[j] = up[int(e) * GU_EXPERT:(int(e) + 1) * GU_EXPERT].cpu().numpy()
+        down_h[j] = down[int(e) * D_EXPERT:(int(e) + 1) * D_EXPERT].cpu().numpy()
+    local = np.searchsorted(sel, ids_np[0, toks]).astype(np.int32)   # [n_tok][K]
+    w = np.full((1, TOP_K), 1.0 / TOP_K, np.float32)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for j in range(n_tok):
+            orc.decode_f32([g.ctypes.data], [u.ctypes.data], [down_h.ctypes.data], GU_EXPERT, D_EXPERT, QT_IQ3_S,
+                           QT_IQ3_S, local[j][None], w, x_np[toks[j], 0], D_MODEL, FF, threads)
+        reps += 1
+        if time.perf_counter() - t0 > 10.0 or reps >= 10:
+            break
+    per_tok = (time.perf_counter() - t0) / reps / n_tok
+    return {"value": round(1.0 / per_tok, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": "%d of the step's tokens (routing set 0), one block each, %d repetitions" % (n_tok, reps)}
+
+
 def cpu_baseline_mixed(gate_p, up_p, down_p, ids_np, w_np, x0_np, n_layers: int = 2):
     """cfg 4's CPU baseline: the oracle's fp32 decode (Q4_K gate/up, Q6_K down)
     of the step's tokens, each through the first n_layers blocks of routing
@@ -901,6 +933,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
         e1.record(stream)
     stream.synchronize()
     e_ms = e0.elapsed_time(e1) / args.steps
+    cpu = None if args.no_cpu_baseline else cpu_baseline_prefill(gate, up, down, ids_np, x.cpu().numpy())
     distinct = np.mean([np.unique(ids_np[s]).size for s in range(PF_SETS)])
     alg_bytes = distinct * (2 * GU_EXPERT + D_EXPERT) + T * D_MODEL * 4 + 2 * T * K * FF * 4 * 2 + T * K * D_MODEL * 4
     flops = 2.0 * T * K * (2 * FF * D_MODEL + D_MODEL * FF)
@@ -928,6 +961,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
                 "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
                 "path": "sabah_rt_mul_mat_id_v2 (C ABI) x3 per step; x and ids from pinned host memory, "
                         "the down output rows back"},
+        "cpu_baseline": cpu,
         "gpu_launches": int(sum(v[0] for v in ktimes.values()) * args.steps),
         "clocks": clk,
         "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3,

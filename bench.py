@@ -775,6 +775,12 @@ def run_ep(args, rank: int, world: int, local_rank: int):
         dist.all_reduce(e_t, op=dist.ReduceOp.MAX)
     e_ms = float(e_t.item())
     assert np.isfinite(out_h.numpy()).all(), "non-finite decode output"
+    # CPU baseline (N = 1 only: the whole bank is on this GPU): the oracle's fp32
+    # decode of one sequence's token through a sample of the 48 blocks, as cfg 2
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(None, [b[0].data_ptr() for b in banks], [b[1].data_ptr() for b in banks],
+                           [b[2].data_ptr() for b in banks], ids_np, w_np, use_ref=False)
     return {
         "metric": EP_METRIC, "value": round(EP_TOKENS * 1e3 / ms_max, 2), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True,
@@ -795,6 +801,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
                 "d2h_bytes_per_step": int(out_h.numel() * 4), "ms_per_step": round(e_ms, 4),
                 "path": "ep.decode_step (C ABI kernels + NCCL), host plans per step in one packed upload"},
         "gpu_launches": int(launches_per_step * args.steps),
+        "cpu_baseline": cpu,
         "clocks": clk,
         "parity": {"rel_l2_vs_fp64": parity, "tol": 2e-3,
                    "checked": "N = 1: routing set 0, all %d blocks, sequences 0-1 (worst), before timing" % LAYERS}
